@@ -1,0 +1,546 @@
+// fpemu_api.cu -- the C ABI of libfpemu.so (declared in include/fpemu.h).
+//
+// Host side of the Ozaki scheme II pipeline: modulus planning and CRT weights
+// (exact integer arithmetic), workspace layout, TMA tensor maps, and the
+// launches of the split, GEMM and CRT kernels.  Nothing here allocates device
+// memory: the caller passes every buffer, including the workspace.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "crt_kernels.cuh"
+#include "gemm_kernel.cuh"
+#include "split_kernels.cuh"
+
+using namespace fpemu;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
+#define FPEMU_CUDA(expr)                                                                        \
+    do {                                                                                        \
+        cudaError_t e_ = (expr);                                                                \
+        if (e_ != cudaSuccess) return fail(FPEMU_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+    } while (0)
+
+#define FPEMU_TRY(expr)              \
+    do {                             \
+        int s_ = (expr);             \
+        if (s_ != FPEMU_OK) return s_; \
+    } while (0)
+
+// The GEMM configuration used by the fused path and the parity taps:
+// 128 x 256 tiles, 4-stage ring of 48 KB, 8 epilogue warps, 2 accumulators
+// (2 x 256 TMEM columns = all 512).
+using MainCfg = GemmCfg<256, 4, 8, 2>;
+
+struct DevInfo {
+    int sms = 0;
+    int major = 0, minor = 0;
+};
+
+int device_info(DevInfo* out) {
+    static std::mutex mu;
+    static DevInfo cache[64];
+    static bool have[64] = {};
+    int dev = 0;
+    FPEMU_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(FPEMU_ERR_NO_DEVICE, "device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lk(mu);
+    if (!have[dev]) {
+        DevInfo d;
+        FPEMU_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+        FPEMU_CUDA(cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev));
+        FPEMU_CUDA(cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev));
+        cache[dev] = d;
+        have[dev] = true;
+    }
+    *out = cache[dev];
+    if (out->major != 10 || out->minor != 0)
+        return fail(FPEMU_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", dev,
+                    out->major, out->minor);
+    return FPEMU_OK;
+}
+
+uint64_t wait_budget_ns() {
+    static uint64_t v = [] {
+        const char* s = getenv("FPEMU_WAIT_BUDGET_MS");
+        long long ms = s ? atoll(s) : 2000;
+        if (ms < 10) ms = 10;
+        return (uint64_t)ms * 1000000ull;
+    }();
+    return v;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+// 3-D map over int8 residues [n_mod][rows][res_ld] (K innermost), box
+// [1][box_rows][128 B], SWIZZLE_128B.  Out-of-range K and rows read as zero.
+int make_residue_map(CUtensorMap* map, const void* base, int64_t k, int64_t rows, int n_mod,
+                     int64_t res_ld, int64_t res_plane, int box_rows) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return fail(FPEMU_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    cuuint64_t dims[3] = {(cuuint64_t)k, (cuuint64_t)rows, (cuuint64_t)n_mod};
+    cuuint64_t strides[2] = {(cuuint64_t)res_ld, (cuuint64_t)res_plane};
+    cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(FPEMU_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d): k=%lld rows=%lld n_mod=%d ld=%lld",
+                    (int)r, (long long)k, (long long)rows, n_mod, (long long)res_ld);
+    return FPEMU_OK;
+}
+
+// ---------------------------------------------------------------- planning --
+
+// Little-endian 32-bit limbs, enough for 2*k*2^(2*bits) and the product of 30 primes.
+struct Big {
+    uint32_t w[10] = {};
+    void mul_small(uint32_t m) {
+        uint64_t carry = 0;
+        for (auto& x : w) {
+            const uint64_t t = (uint64_t)x * m + carry;
+            x = (uint32_t)t;
+            carry = t >> 32;
+        }
+    }
+    static int cmp(const Big& a, const Big& b) {
+        for (int i = 9; i >= 0; --i)
+            if (a.w[i] != b.w[i]) return a.w[i] < b.w[i] ? -1 : 1;
+        return 0;
+    }
+};
+
+int plan_moduli(int64_t k, int bits, int* n_mod) {
+    if (k < 0 || bits < 1 || bits > 64) return fail(FPEMU_ERR_INVALID, "plan_moduli: k=%lld bits=%d", (long long)k, bits);
+    // target = 2 * k * 2^(2*bits)
+    Big target;
+    const int sh = 2 * bits + 1;
+    const unsigned __int128 kk = (unsigned __int128)(uint64_t)k;
+    for (int i = 0; i < 10; ++i) {
+        const int lo_bit = 32 * i - sh;  // bit of k that lands at limb i bit 0
+        unsigned __int128 v;
+        if (lo_bit >= 0) v = lo_bit >= 128 ? 0 : (kk >> lo_bit);
+        else v = (-lo_bit) >= 128 ? 0 : (kk << (-lo_bit));
+        target.w[i] = (uint32_t)v;
+    }
+    Big prod;
+    prod.w[0] = 1;
+    for (int i = 0; i < kNumPrimes; ++i) {
+        prod.mul_small((uint32_t)kPrimes[i]);
+        if (Big::cmp(prod, target) > 0) {
+            *n_mod = i + 1;
+            return FPEMU_OK;
+        }
+    }
+    return fail(FPEMU_ERR_NO_MODULI, "not enough primes for inner dim %lld, bits %d", (long long)k, bits);
+}
+
+typedef unsigned __int128 u128;
+typedef __int128 i128;
+
+int crt_weights(int n_mod, CrtConsts* c) {
+    if (n_mod < 1 || n_mod > kMaxModuli)
+        return fail(FPEMU_ERR_UNSUPPORTED, "n_mod=%d outside [1, %d]", n_mod, kMaxModuli);
+    u128 M = 1;
+    for (int i = 0; i < n_mod; ++i) M *= (u128)kPrimes[i];  // < 2^127 for n_mod <= 25
+    for (int i = 0; i < n_mod; ++i) {
+        const uint32_t p = (uint32_t)kPrimes[i];
+        const u128 Mi = M / p;
+        const uint32_t a = (uint32_t)(Mi % p);
+        uint32_t inv = 0;
+        for (uint32_t t = 1; t < p; ++t)
+            if ((a * t) % p == 1) { inv = t; break; }
+        const u128 w = Mi * inv;  // < M
+        const double hi = (double)w;
+        const i128 r = (i128)w - (i128)hi;
+        const double mid = (double)r;
+        const double lo = (double)(r - (i128)mid);
+        c->wh[i] = hi;
+        c->wm[i] = mid;
+        c->wl[i] = lo;
+    }
+    c->M_hi = (double)M;
+    c->M_lo = (double)((i128)M - (i128)c->M_hi);
+    c->inv_M = 1.0 / c->M_hi;
+    return FPEMU_OK;
+}
+
+void mod_consts(int n_mod, ModConsts* mc) {
+    memset(mc, 0, sizeof *mc);
+    for (int i = 0; i < n_mod; ++i) {
+        const uint32_t p = (uint32_t)kPrimes[i];
+        uint32_t s = 0;
+        while ((2u << s) <= p) ++s;  // floor(log2 p)
+        const uint64_t num = 1ull << (32 + s);
+        mc->p[i] = p;
+        mc->shift[i] = s;
+        mc->magic[i] = (uint32_t)((num + p - 1) / p);
+        mc->c18[i] = (uint32_t)((1ull << 18) % p);
+        mc->c36[i] = (uint32_t)((1ull << 36) % p);
+        mc->kneg[i] = p << 24;
+    }
+}
+
+int64_t max_k(int n_mod) {
+    if (n_mod < 1 || n_mod > kMaxModuli) return 0;
+    const int64_t pm = kPrimes[n_mod - 1] - 1;
+    return (int64_t)2147483647 / (pm * pm);
+}
+
+// ------------------------------------------------------------- workspace --
+
+inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+inline int64_t res_ld_for(int64_t k) { return ((k + 15) / 16) * 16; }
+
+int gemm_grid(const DevInfo& d, int64_t m, int64_t n) {
+    const int64_t tiles = ((m + kBM - 1) / kBM) * ((n + MainCfg::BN - 1) / MainCfg::BN);
+    return (int)(tiles < d.sms ? tiles : d.sms);
+}
+
+size_t gemm_scratch_bytes(const DevInfo& d, int64_t m, int64_t n, int n_mod) {
+    return align256((size_t)gemm_grid(d, m, n) * (size_t)MainCfg::scratch_per_cta(n_mod));
+}
+
+struct Layout {
+    int64_t res_ld;
+    size_t a_res, b_res, row_exp, col_exp, colmax, scratch, total;
+};
+
+Layout layout(const DevInfo& d, int64_t m, int64_t n, int64_t k, int n_mod) {
+    Layout L;
+    L.res_ld = res_ld_for(k);
+    size_t off = 0;
+    L.a_res = off; off += align256((size_t)n_mod * m * L.res_ld);
+    L.b_res = off; off += align256((size_t)n_mod * n * L.res_ld);
+    L.row_exp = off; off += align256((size_t)m * 4);
+    L.col_exp = off; off += align256((size_t)n * 4);
+    L.colmax = off; off += align256((size_t)(m > n ? m : n) * 8);
+    L.scratch = off; off += gemm_scratch_bytes(d, m, n, n_mod);
+    L.total = off;
+    return L;
+}
+
+// ---------------------------------------------------------------- launches --
+
+int launch_split(const SplitParams& P, uint64_t* colmax, const DevInfo& d, cudaStream_t st) {
+    if (P.rows == 0) return FPEMU_OK;
+    if (P.s_k == 1) {
+        const bool vec = (reinterpret_cast<uintptr_t>(P.X) % 16 == 0) && (P.s_row % 2 == 0 || P.rows == 1);
+        const int group = P.k <= 512 ? 32 : P.k <= 2048 ? 64 : P.k <= 8192 ? 128 : 256;
+        const int64_t rows_per_cta = 256 / group;
+        int64_t grid = (P.rows + rows_per_cta - 1) / rows_per_cta;
+        const int64_t cap = (int64_t)d.sms * 64;
+        if (grid > cap) grid = cap;
+#define FPEMU_SPLIT_ROWS(G)                                                                     \
+    do {                                                                                        \
+        if (vec) split_rows_kernel<G, true><<<(unsigned)grid, 256, 0, st>>>(P);                 \
+        else split_rows_kernel<G, false><<<(unsigned)grid, 256, 0, st>>>(P);                    \
+    } while (0)
+        switch (group) {
+            case 32: FPEMU_SPLIT_ROWS(32); break;
+            case 64: FPEMU_SPLIT_ROWS(64); break;
+            case 128: FPEMU_SPLIT_ROWS(128); break;
+            default: FPEMU_SPLIT_ROWS(256); break;
+        }
+#undef FPEMU_SPLIT_ROWS
+    } else {
+        if (colmax == nullptr) return fail(FPEMU_ERR_INVALID, "split: strided K needs colmax scratch");
+        FPEMU_CUDA(cudaMemsetAsync(colmax, 0, (size_t)P.rows * 8, st));
+        dim3 g1((unsigned)((P.rows + 255) / 256), (unsigned)((P.k + kColmaxK - 1) / kColmaxK));
+        split_colmax_kernel<<<g1, 256, 0, st>>>(P, reinterpret_cast<unsigned long long*>(colmax));
+        FPEMU_CUDA(cudaGetLastError());
+        SplitParams Q = P;
+        Q.colmax = colmax;
+        dim3 g2((unsigned)((P.rows + kTileR - 1) / kTileR), (unsigned)((P.res_ld + kTileK - 1) / kTileK));
+        split_strided_kernel<<<g2, 256, 0, st>>>(Q);
+    }
+    FPEMU_CUDA(cudaGetLastError());
+    return FPEMU_OK;
+}
+
+template <int MODE>
+int launch_gemm(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int64_t res_ld, const DevInfo& d,
+                cudaStream_t st) {
+    const int64_t m = P.m, n = P.n;
+    if (m == 0 || n == 0) return FPEMU_OK;
+    const int64_t res_plane_a = m * res_ld, res_plane_b = n * res_ld;
+    CUtensorMap ta, tb;
+    FPEMU_TRY(make_residue_map(&ta, a_res, P.k, m, P.n_mod, res_ld, res_plane_a, kBM));
+    FPEMU_TRY(make_residue_map(&tb, b_res, P.k, n, P.n_mod, res_ld, res_plane_b, MainCfg::BN));
+    P.num_kb = (int)((P.k + kBK - 1) / kBK);
+    P.tiles_m = (int)((m + kBM - 1) / kBM);
+    P.tiles_n = (int)((n + MainCfg::BN - 1) / MainCfg::BN);
+    P.num_tiles = P.tiles_m * P.tiles_n;
+    P.budget_ns = wait_budget_ns();
+    mod_consts(P.n_mod, &P.mc);
+    const int grid = gemm_grid(d, m, n);
+    auto kern = ozaki_gemm_kernel<MainCfg, MODE>;
+    FPEMU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MainCfg::kSmemBytes));
+    kern<<<grid, MainCfg::kThreads, MainCfg::kSmemBytes, st>>>(ta, tb, P);
+    FPEMU_CUDA(cudaGetLastError());
+    return FPEMU_OK;
+}
+
+int check_gemm_args(int64_t m, int64_t n, int64_t k, int n_mod, const void* a_res, const void* b_res,
+                    int64_t res_ld) {
+    if (m < 0 || n < 0 || k < 1) return fail(FPEMU_ERR_INVALID, "bad sizes m=%lld n=%lld k=%lld", (long long)m, (long long)n, (long long)k);
+    if (n_mod < 1 || n_mod > kMaxModuli) return fail(FPEMU_ERR_UNSUPPORTED, "n_mod=%d outside [1, %d]", n_mod, kMaxModuli);
+    if (k > max_k(n_mod))
+        return fail(FPEMU_ERR_UNSUPPORTED, "k=%lld exceeds the exact int32 accumulation limit %lld for n_mod=%d",
+                    (long long)k, (long long)max_k(n_mod), n_mod);
+    if (m > 0x7FFFFFFFll || n > 0x7FFFFFFFll) return fail(FPEMU_ERR_UNSUPPORTED, "m or n beyond 2^31-1");
+    if (res_ld < k || res_ld % 16 != 0) return fail(FPEMU_ERR_INVALID, "res_ld=%lld must be >= k and a multiple of 16", (long long)res_ld);
+    if ((m > 0 && n > 0) && (a_res == nullptr || b_res == nullptr)) return fail(FPEMU_ERR_INVALID, "null residue pointer");
+    if ((reinterpret_cast<uintptr_t>(a_res) | reinterpret_cast<uintptr_t>(b_res)) % 16 != 0)
+        return fail(FPEMU_ERR_INVALID, "residue buffers must be 16-byte aligned");
+    return FPEMU_OK;
+}
+
+int bits_ok(int bits) {
+    if (bits < 1 || bits > 53) return fail(FPEMU_ERR_INVALID, "bits=%d outside [1, 53]", bits);
+    return FPEMU_OK;
+}
+
+}  // namespace
+
+// ==================================================================== C ABI ==
+
+extern "C" {
+
+const char* fpemu_status_string(int status) {
+    switch (status) {
+        case FPEMU_OK: return "ok";
+        case FPEMU_ERR_INVALID: return "invalid argument";
+        case FPEMU_ERR_NO_MODULI: return "not enough primes";
+        case FPEMU_ERR_UNSUPPORTED: return "unsupported problem";
+        case FPEMU_ERR_WORKSPACE: return "workspace too small or misaligned";
+        case FPEMU_ERR_CUDA: return "CUDA error";
+        case FPEMU_ERR_TIMEOUT: return "device wait timed out";
+        case FPEMU_ERR_NO_DEVICE: return "unsupported device";
+        default: return "unknown status";
+    }
+}
+
+const char* fpemu_last_error(void) { return t_last_error.c_str(); }
+
+int fpemu_abi_version(void) { return FPEMU_ABI_VERSION; }
+
+int fpemu_plan_moduli(int64_t k, int bits, int* n_mod, int32_t* moduli) {
+    if (n_mod == nullptr) return fail(FPEMU_ERR_INVALID, "n_mod is null");
+    FPEMU_TRY(plan_moduli(k, bits, n_mod));
+    if (moduli)
+        for (int i = 0; i < *n_mod; ++i) moduli[i] = kPrimes[i];
+    return FPEMU_OK;
+}
+
+int fpemu_crt_weights(int n_mod, double* wh, double* wm, double* wl, double* M_hi, double* M_lo,
+                      double* inv_M) {
+    if (!wh || !wm || !wl || !M_hi || !M_lo || !inv_M) return fail(FPEMU_ERR_INVALID, "null output");
+    CrtConsts c;
+    FPEMU_TRY(crt_weights(n_mod, &c));
+    for (int i = 0; i < n_mod; ++i) {
+        wh[i] = c.wh[i];
+        wm[i] = c.wm[i];
+        wl[i] = c.wl[i];
+    }
+    *M_hi = c.M_hi;
+    *M_lo = c.M_lo;
+    *inv_M = c.inv_M;
+    return FPEMU_OK;
+}
+
+int64_t fpemu_max_k(int n_mod) { return max_k(n_mod); }
+
+size_t fpemu_gemm_workspace_size(int64_t m, int64_t n, int n_mod) {
+    DevInfo d;
+    if (device_info(&d) != FPEMU_OK || m < 0 || n < 0 || n_mod < 1 || n_mod > kMaxModuli) return 0;
+    return gemm_scratch_bytes(d, m, n, n_mod);
+}
+
+size_t fpemu_workspace_size(int64_t m, int64_t n, int64_t k, int n_mod) {
+    DevInfo d;
+    if (device_info(&d) != FPEMU_OK || m < 0 || n < 0 || k < 1 || n_mod < 1 || n_mod > kMaxModuli) return 0;
+    return layout(d, m, n, k, n_mod).total;
+}
+
+int fpemu_split(int64_t rows, int64_t k, const double* X, int64_t s_row, int64_t s_k, int bits, int n_mod,
+                int8_t* res, int64_t res_ld, int64_t res_plane, int32_t* exps, uint64_t* colmax_scratch,
+                void* stream) {
+    DevInfo d;
+    FPEMU_TRY(device_info(&d));
+    FPEMU_TRY(bits_ok(bits));
+    if (rows < 0 || k < 1 || s_row < 0 || s_k < 0) return fail(FPEMU_ERR_INVALID, "split: bad sizes or strides");
+    if (n_mod < 1 || n_mod > kMaxModuli) return fail(FPEMU_ERR_UNSUPPORTED, "n_mod=%d outside [1, %d]", n_mod, kMaxModuli);
+    if (res_ld < k || res_ld % 16 != 0 || res_plane < rows * res_ld || res_plane % 16 != 0)
+        return fail(FPEMU_ERR_INVALID, "split: res_ld must be a multiple of 16 >= k, res_plane >= rows*res_ld");
+    if (rows > 0 && (!X || !res || !exps)) return fail(FPEMU_ERR_INVALID, "split: null pointer");
+    if (reinterpret_cast<uintptr_t>(res) % 16 != 0) return fail(FPEMU_ERR_INVALID, "split: res not 16-byte aligned");
+    SplitParams P;
+    memset(&P, 0, sizeof P);
+    P.X = X;
+    P.rows = rows;
+    P.k = k;
+    P.s_row = s_row;
+    P.s_k = s_k;
+    P.res = res;
+    P.res_ld = res_ld;
+    P.res_plane = res_plane;
+    P.exps = exps;
+    P.bits = bits;
+    P.n_mod = n_mod;
+    mod_consts(n_mod, &P.mc);
+    return launch_split(P, colmax_scratch, d, static_cast<cudaStream_t>(stream));
+}
+
+int fpemu_gemm_residues(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_res, const int8_t* b_res,
+                        int64_t res_ld, int mode, void* out, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+    (void)workspace;
+    (void)workspace_bytes;
+    DevInfo d;
+    FPEMU_TRY(device_info(&d));
+    FPEMU_TRY(check_gemm_args(m, n, k, n_mod, a_res, b_res, res_ld));
+    if (mode != 0 && mode != 1) return fail(FPEMU_ERR_INVALID, "mode must be 0 (raw) or 1 (residues)");
+    if (m > 0 && n > 0 && out == nullptr) return fail(FPEMU_ERR_INVALID, "null output");
+    GemmParams P;
+    memset(&P, 0, sizeof P);
+    P.m = (int)m;
+    P.n = (int)n;
+    P.k = (int)k;
+    P.n_mod = n_mod;
+    P.out = out;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return mode == 0 ? launch_gemm<kModeRaw>(P, a_res, b_res, res_ld, d, st)
+                     : launch_gemm<kModeResidue>(P, a_res, b_res, res_ld, d, st);
+}
+
+int fpemu_crt_reconstruct(int64_t m, int64_t n, int n_mod, const uint8_t* res, const int32_t* row_exp,
+                          const int32_t* col_exp, int bits, double* C, int64_t ldc, void* stream) {
+    DevInfo d;
+    FPEMU_TRY(device_info(&d));
+    FPEMU_TRY(bits_ok(bits));
+    if (m < 0 || n < 0 || ldc < n) return fail(FPEMU_ERR_INVALID, "crt: bad sizes");
+    if (m == 0 || n == 0) return FPEMU_OK;
+    if (!res || !row_exp || !col_exp || !C) return fail(FPEMU_ERR_INVALID, "crt: null pointer");
+    CrtConsts cc;
+    FPEMU_TRY(crt_weights(n_mod, &cc));
+    const int64_t work = m * ((n + 3) / 4);
+    int64_t grid = (work + 255) / 256;
+    if (grid > (int64_t)d.sms * 32) grid = (int64_t)d.sms * 32;
+    crt_kernel<<<(unsigned)grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(res, m, n, n_mod, row_exp, col_exp,
+                                                                           2 * bits, C, ldc, cc);
+    FPEMU_CUDA(cudaGetLastError());
+    return FPEMU_OK;
+}
+
+int fpemu_gemm_crt(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_res, const int8_t* b_res,
+                   int64_t res_ld, const int32_t* row_exp, const int32_t* col_exp, int bits, double* C,
+                   int64_t ldc, void* workspace, size_t workspace_bytes, void* stream) {
+    DevInfo d;
+    FPEMU_TRY(device_info(&d));
+    FPEMU_TRY(bits_ok(bits));
+    FPEMU_TRY(check_gemm_args(m, n, k, n_mod, a_res, b_res, res_ld));
+    if (m == 0 || n == 0) return FPEMU_OK;
+    if (!row_exp || !col_exp || !C || ldc < n) return fail(FPEMU_ERR_INVALID, "gemm_crt: bad output arguments");
+    const size_t need = gemm_scratch_bytes(d, m, n, n_mod);
+    if (workspace == nullptr || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+        return fail(FPEMU_ERR_WORKSPACE, "gemm_crt: need %zu bytes of 256-byte aligned workspace, got %zu",
+                    need, workspace_bytes);
+    GemmParams P;
+    memset(&P, 0, sizeof P);
+    P.m = (int)m;
+    P.n = (int)n;
+    P.k = (int)k;
+    P.n_mod = n_mod;
+    P.C = C;
+    P.ldc = ldc;
+    P.row_exp = row_exp;
+    P.col_exp = col_exp;
+    P.two_bits = 2 * bits;
+    P.scratch = static_cast<uint8_t*>(workspace);
+    P.scratch_per_cta = MainCfg::scratch_per_cta(n_mod);
+    FPEMU_TRY(crt_weights(n_mod, &P.cc));
+    return launch_gemm<kModeCrt>(P, a_res, b_res, res_ld, d, static_cast<cudaStream_t>(stream));
+}
+
+int fpemu_ozaki2_dgemm(int64_t m, int64_t n, int64_t k, const double* A, int64_t sA_row, int64_t sA_col,
+                       const double* B, int64_t sB_row, int64_t sB_col, double* C, int64_t ldc, int bits,
+                       int n_mod, void* workspace, size_t workspace_bytes, void* stream) {
+    DevInfo d;
+    FPEMU_TRY(device_info(&d));
+    FPEMU_TRY(bits_ok(bits));
+    if (m < 0 || n < 0 || k < 1) return fail(FPEMU_ERR_INVALID, "bad sizes m=%lld n=%lld k=%lld", (long long)m, (long long)n, (long long)k);
+    if (sA_row < 0 || sA_col < 0 || sB_row < 0 || sB_col < 0 || ldc < n)
+        return fail(FPEMU_ERR_INVALID, "negative stride or ldc < n");
+    if (m == 0 || n == 0) return FPEMU_OK;
+    if (!A || !B || !C) return fail(FPEMU_ERR_INVALID, "null matrix pointer");
+    if (n_mod == 0) FPEMU_TRY(plan_moduli(k, bits, &n_mod));
+    if (n_mod < 1 || n_mod > kMaxModuli) return fail(FPEMU_ERR_UNSUPPORTED, "n_mod=%d outside [1, %d]", n_mod, kMaxModuli);
+    if (k > max_k(n_mod))
+        return fail(FPEMU_ERR_UNSUPPORTED, "k=%lld exceeds the exact int32 accumulation limit %lld",
+                    (long long)k, (long long)max_k(n_mod));
+    const Layout L = layout(d, m, n, k, n_mod);
+    if (workspace == nullptr || workspace_bytes < L.total || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+        return fail(FPEMU_ERR_WORKSPACE, "need %zu bytes of 256-byte aligned workspace, got %zu", L.total,
+                    workspace_bytes);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    int8_t* a_res = reinterpret_cast<int8_t*>(ws + L.a_res);
+    int8_t* b_res = reinterpret_cast<int8_t*>(ws + L.b_res);
+    int32_t* re = reinterpret_cast<int32_t*>(ws + L.row_exp);
+    int32_t* ce = reinterpret_cast<int32_t*>(ws + L.col_exp);
+    uint64_t* colmax = reinterpret_cast<uint64_t*>(ws + L.colmax);
+    FPEMU_TRY(fpemu_split(m, k, A, sA_row, sA_col, bits, n_mod, a_res, L.res_ld, m * L.res_ld, re, colmax, stream));
+    FPEMU_TRY(fpemu_split(n, k, B, sB_col, sB_row, bits, n_mod, b_res, L.res_ld, n * L.res_ld, ce, colmax, stream));
+    return fpemu_gemm_crt(m, n, k, n_mod, a_res, b_res, L.res_ld, re, ce, bits, C, ldc, ws + L.scratch,
+                          L.total - L.scratch, stream);
+}
+
+int fpemu_device_error(int* code, int* where, int* block, int* detail, int clear) {
+    if (code == nullptr) return fail(FPEMU_ERR_INVALID, "code is null");
+    FPEMU_CUDA(cudaDeviceSynchronize());
+    DeviceError e;
+    FPEMU_CUDA(cudaMemcpyFromSymbol(&e, g_device_error, sizeof e));
+    *code = e.code;
+    if (where) *where = e.where;
+    if (block) *block = e.block;
+    if (detail) *detail = e.detail;
+    if (clear) {
+        DeviceError z;
+        memset(&z, 0, sizeof z);
+        FPEMU_CUDA(cudaMemcpyToSymbol(g_device_error, &z, sizeof z));
+    }
+    return FPEMU_OK;
+}
+
+}  // extern "C"

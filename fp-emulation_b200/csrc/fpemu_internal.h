@@ -1,0 +1,67 @@
+// fpemu_internal.h -- structures shared by the host API and the kernels.
+#pragma once
+
+#include <stdint.h>
+
+#include "../../include/fpemu.h"
+
+namespace fpemu {
+
+constexpr int kMaxModuli = 25;  // 25 primes cover k <= 214748 at 53 bits (int32 limit)
+constexpr int kNumPrimes = 30;
+constexpr int kPrimes[kNumPrimes] = {3,  5,  7,  11, 13, 17, 19, 23, 29, 31,  37,  41,  43,  47,  53,
+                                     59, 61, 67, 71, 73, 79, 83, 89, 97, 101, 103, 107, 109, 113, 127};
+
+// Row/column exponent recorded for a row or column that holds NaN or +-Inf;
+// every output element that depends on it becomes NaN.
+constexpr int kNonFiniteExp = -0x40000000;
+
+// Per-modulus integer constants (see mod_small in fpemu_device.cuh).
+struct ModConsts {
+    uint32_t p[kMaxModuli];
+    uint32_t magic[kMaxModuli];
+    uint32_t shift[kMaxModuli];
+    uint32_t c18[kMaxModuli];
+    uint32_t c36[kMaxModuli];
+    uint32_t kneg[kMaxModuli];
+};
+
+// CRT constants, ozaki.py:62-80.
+struct CrtConsts {
+    double wh[kMaxModuli];
+    double wm[kMaxModuli];
+    double wl[kMaxModuli];
+    double M_hi, M_lo, inv_M;
+};
+
+struct SplitParams {
+    const double* X;
+    int64_t rows, k, s_row, s_k;
+    int8_t* res;
+    int64_t res_ld, res_plane;
+    int32_t* exps;
+    const uint64_t* colmax;  // strided variant only
+    int bits, n_mod;
+    ModConsts mc;
+};
+
+enum GemmMode : int { kModeRaw = 0, kModeResidue = 1, kModeCrt = 2 };
+
+struct GemmParams {
+    int m, n, k, n_mod;
+    int num_kb;            // ceil(k / 128)
+    int tiles_m, tiles_n, num_tiles;
+    void* out;             // raw int32 / uint8 residues, [n_mod][m][n] (modes 0, 1)
+    double* C;             // mode 2
+    int64_t ldc;
+    const int32_t* row_exp;
+    const int32_t* col_exp;
+    int two_bits;
+    uint8_t* scratch;      // mode 2: per-CTA residue staging
+    int64_t scratch_per_cta;
+    uint64_t budget_ns;    // bound on every mbarrier wait
+    ModConsts mc;
+    CrtConsts cc;
+};
+
+}  // namespace fpemu

@@ -1,0 +1,318 @@
+// gemm_kernel.cuh -- the per-modulus INT8 GEMMs of Ozaki scheme II as ONE
+// persistent, warp-specialised tcgen05 kernel (replaces the reference's
+// cuBLASLt strided-batched GEMM + mod_reduce + crt_kernel, crt_kernel.cu:6-146).
+//
+// Work: output tiles of 128 x BN; a CTA takes tiles round-robin and, for each
+// tile, runs the full K loop once per modulus l = 0 .. n_mod-1 (tile-major), so
+// all residues of a tile are produced by one CTA back to back.
+//
+// Roles (one CTA per SM):
+//   warp 0, one thread   TMA producer: A and B residue tiles [128 x 128 B] and
+//                        [BN x 128 B] (SWIZZLE_128B) into a STAGES-deep ring.
+//   warp 1, one thread   MMA issuer: 4 x tcgen05.mma.kind::i8 (K = 32 each) per
+//                        stage into an int32 accumulator in TMEM; NACC
+//                        accumulator buffers let the epilogue drain one while
+//                        the next modulus accumulates.  Warp 1 owns TMEM.
+//   warps 2 .. 2+NEPI    epilogue: tcgen05.ld the accumulator (each warp reads
+//                        its TMEM lane quadrant, warp % 4), reduce mod p_l, and
+//                          mode 0: store raw int32 products     (parity tap)
+//                          mode 1: store uint8 residues          (parity tap)
+//                          mode 2: stage uint8 residues in this thread's slice
+//                                  of the CTA's scratch; after the last modulus
+//                                  run the CRT for the thread's row segment and
+//                                  write FP64 C.
+//
+// Every wait is bounded (mbar_wait): on timeout the CTA records the error,
+// raises a shared abort flag, drains its in-flight TMA loads and MMAs, frees
+// TMEM and exits.  No TMA multicast is used.
+#pragma once
+
+#include "crt_kernels.cuh"
+
+namespace fpemu {
+
+constexpr int kBM = 128;       // tile rows (TMEM lanes)
+constexpr int kBK = 128;       // K bytes per stage: one 128-byte swizzle row
+constexpr int kUmmaK = 32;     // K of one tcgen05.mma kind::i8
+constexpr int kBandRows = 16;  // tile rows per raster band (L2 reuse of A and B)
+
+template <int BN_, int STAGES_, int NEPI_, int NACC_>
+struct GemmCfg {
+    static constexpr int BN = BN_, STAGES = STAGES_, NEPI = NEPI_, NACC = NACC_;
+    static constexpr int kStageA = kBM * kBK;
+    static constexpr int kStageB = BN * kBK;
+    static constexpr int kThreads = 32 * (2 + NEPI);
+    static constexpr int kTmemCols = NACC * BN;
+    static constexpr int kColGroups = NEPI / 4;    // epilogue warps per lane quadrant
+    static constexpr int kCols = BN / kColGroups;  // accumulator columns per epilogue thread
+    static constexpr int kChunks = kCols / 32;     // 32-column TMEM loads per thread
+    static constexpr int kBarBytes = 8 * (2 * STAGES + 2 * NACC + 1) + 16;
+    static constexpr int kSmemBytes = 1024 + STAGES * (kStageA + kStageB) + kBarBytes;
+    static_assert(NEPI % 4 == 0 && kCols % 32 == 0, "epilogue split");
+    static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "UMMA N for M = 128");
+    static_assert(kTmemCols == 32 || kTmemCols == 64 || kTmemCols == 128 || kTmemCols == 256 ||
+                      kTmemCols == 512,
+                  "TMEM allocation must be a power of two in [32, 512]");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+    // Residue staging for mode 2: every epilogue thread owns n_mod * kCols bytes.
+    static int64_t scratch_per_cta(int n_mod) { return (int64_t)n_mod * kBM * BN; }
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
+    const int per_band = kBandRows * tiles_n;
+    const int band = tile / per_band;
+    const int r = tile - band * per_band;
+    const int first = band * kBandRows;
+    const int rows = min(tiles_m - first, kBandRows);
+    tm = first + r % rows;
+    tn = r / rows;
+}
+
+__device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    return a | (b << 8) | (c << 16) | (d << 24);
+}
+
+template <class Cfg, int MODE>
+__global__ void __launch_bounds__(Cfg::kThreads, 1)
+    ozaki_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ GemmParams P) {
+    constexpr int BN = Cfg::BN, STAGES = Cfg::STAGES, NACC = Cfg::NACC;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * Cfg::kStageA;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::kStageB);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + NACC;
+    uint64_t* drain = tempty + NACC;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
+        }
+        for (int a = 0; a < NACC; ++a) {
+            mbar_init(tfull + a, 1);
+            mbar_init(tempty + a, Cfg::NEPI);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            int stage = 0, issued = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < P.num_tiles; tile += gridDim.x) {
+                int tm, tn;
+                tile_coords(tile, P.tiles_m, P.tiles_n, tm, tn);
+                for (int l = 0; ok && l < P.n_mod; ++l) {
+                    for (int kb = 0; kb < P.num_kb; ++kb) {
+                        if (*abort_flag) { ok = false; break; }
+                        if (!mbar_wait(empty + stage, ph ^ 1u, P.budget_ns)) {
+                            report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitEmpty, tile);
+                            *abort_flag = 1;
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(full + stage, Cfg::kStageA + Cfg::kStageB);
+                        tma_load_3d(sA + stage * Cfg::kStageA, &tmA, full + stage, kb * kBK, tm * kBM, l);
+                        tma_load_3d(sB + stage * Cfg::kStageB, &tmB, full + stage, kb * kBK, tn * BN, l);
+                        ++issued;
+                        if (++stage == STAGES) { stage = 0; ph ^= 1u; }
+                    }
+                }
+            }
+            // Loads still in flight must land before this CTA's shared memory goes away.
+            const int outstanding = issued < STAGES ? issued : STAGES;
+            for (int i = 0; i < outstanding; ++i) {
+                if (--stage < 0) { stage = STAGES - 1; ph ^= 1u; }
+                if (!mbar_wait(full + stage, ph, P.budget_ns)) {
+                    report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitDrainTma, stage);
+                    *abort_flag = 1;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t kIdesc = idesc_i8(kBM, BN);
+            int stage = 0, acc = 0;
+            uint32_t ph = 0, aph = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < P.num_tiles; tile += gridDim.x) {
+                for (int l = 0; ok && l < P.n_mod; ++l) {
+                    if (*abort_flag) { ok = false; break; }
+                    if (!mbar_wait(tempty + acc, aph ^ 1u, P.budget_ns)) {
+                        report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitTmemEmpty, tile);
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                    for (int kb = 0; kb < P.num_kb; ++kb) {
+                        if (!mbar_wait(full + stage, ph, P.budget_ns)) {
+                            report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitFull, tile);
+                            *abort_flag = 1;
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a0 = smem_u32(sA + stage * Cfg::kStageA);
+                        const uint32_t b0 = smem_u32(sB + stage * Cfg::kStageB);
+#pragma unroll
+                        for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+                            mma_i8(d_tmem, smem_desc_k_sw128(a0 + kk * kUmmaK),
+                                   smem_desc_k_sw128(b0 + kk * kUmmaK), kIdesc,
+                                   (kb | kk) != 0 ? 1u : 0u);
+                        }
+                        mma_commit(empty + stage);  // frees the stage once these MMAs finish
+                        if (++stage == STAGES) { stage = 0; ph ^= 1u; }
+                    }
+                    if (!ok) break;
+                    mma_commit(tfull + acc);  // accumulator complete
+                    if (++acc == NACC) { acc = 0; aph ^= 1u; }
+                }
+            }
+            // Every MMA issued above must finish before TMEM is released.
+            mma_commit(drain);
+            if (!mbar_wait(drain, 0, P.budget_ns)) {
+                report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitDrainMma, 0);
+                *abort_flag = 1;
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int ew = warp - 2;
+        const int quad = warp & 3;  // TMEM lanes this warp may read: [32*quad, 32*quad + 32)
+        const int cg = ew >> 2;     // which kCols-wide slice of the tile
+        const int row_in_tile = quad * 32 + lane;
+        uint8_t* scr = nullptr;
+        if (MODE == kModeCrt)
+            scr = P.scratch + (int64_t)blockIdx.x * P.scratch_per_cta +
+                  ((int64_t)ew * P.n_mod * Cfg::kChunks * 32 + lane) * 32;
+        int acc = 0;
+        uint32_t aph = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && tile < P.num_tiles; tile += gridDim.x) {
+            int tm, tn;
+            tile_coords(tile, P.tiles_m, P.tiles_n, tm, tn);
+            const int64_t row = (int64_t)tm * kBM + row_in_tile;
+            const int col0 = tn * BN + cg * Cfg::kCols;
+            for (int l = 0; l < P.n_mod; ++l) {
+                if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
+                bool got = mbar_wait(tfull + acc, aph, P.budget_ns);
+                got = __all_sync(0xffffffffu, got);
+                if (!got) {
+                    if (lane == 0) report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitTmemFull, tile);
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t taddr =
+                    tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + cg * Cfg::kCols);
+                const uint32_t p = P.mc.p[l], mg = P.mc.magic[l], sh = P.mc.shift[l];
+#pragma unroll 1
+                for (int c = 0; c < Cfg::kChunks; ++c) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), v);
+                    tmem_ld_wait();
+                    const int cb = col0 + c * 32;
+                    if (MODE == kModeRaw) {
+                        if (row < P.m) {
+                            int32_t* o = static_cast<int32_t*>(P.out) + ((int64_t)l * P.m + row) * P.n;
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (cb + j < P.n) o[cb + j] = (int32_t)v[j];
+                        }
+                    } else {
+                        uint32_t w[8];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            w[q] = pack4(mod_small(v[4 * q], p, mg, sh), mod_small(v[4 * q + 1], p, mg, sh),
+                                         mod_small(v[4 * q + 2], p, mg, sh), mod_small(v[4 * q + 3], p, mg, sh));
+                        if (MODE == kModeResidue) {
+                            if (row < P.m) {
+                                uint8_t* o = static_cast<uint8_t*>(P.out) + ((int64_t)l * P.m + row) * P.n;
+#pragma unroll
+                                for (int j = 0; j < 32; ++j)
+                                    if (cb + j < P.n) o[cb + j] = (uint8_t)(w[j >> 2] >> (8 * (j & 3)));
+                            }
+                        } else {
+                            uint4* d = reinterpret_cast<uint4*>(scr + ((int64_t)l * Cfg::kChunks + c) * 1024);
+                            d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                            d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(tempty + acc);
+                if (++acc == NACC) { acc = 0; aph ^= 1u; }
+            }
+            if (!ok) break;
+            if (MODE == kModeCrt && row < P.m) {
+                // CRT for this thread's row segment: kCols columns, 16 at a time,
+                // from the residues it staged for every modulus.
+                const int re = P.row_exp[row];
+                double* crow = P.C + row * P.ldc;
+#pragma unroll 1
+                for (int h = 0; h < Cfg::kChunks * 2; ++h) {
+                    const int cb = col0 + h * 16;
+                    if (cb >= P.n) break;
+                    double hi[16], lo[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) { hi[j] = 0.0; lo[j] = 0.0; }
+                    const uint8_t* src = scr + (int64_t)(h >> 1) * 1024 + (h & 1) * 16;
+#pragma unroll 1
+                    for (int l = 0; l < P.n_mod; ++l) {
+                        const uint4 q = *reinterpret_cast<const uint4*>(src + (int64_t)l * Cfg::kChunks * 1024);
+                        const double wh = P.cc.wh[l], wm = P.cc.wm[l], wl = P.cc.wl[l];
+                        const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            crt_step((double)((qq[j >> 2] >> (8 * (j & 3))) & 0xFFu), wh, wm, wl, hi[j], lo[j]);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int col = cb + j;
+                        if (col < P.n)
+                            crow[col] = crt_scale(crt_finish(hi[j], lo[j], P.cc), re, P.col_exp[col], P.two_bits);
+                    }
+                }
+            }
+        }
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+}  // namespace fpemu

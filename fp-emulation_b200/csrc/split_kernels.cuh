@@ -1,0 +1,242 @@
+// split_kernels.cuh -- the fused scale/split step (ozaki.py:32-46 of the
+// reference): per row of an operand, the power-of-two exponent of its largest
+// magnitude, the exact scaling to a 53-bit (or `bits`-bit) integer with
+// round-half-even, and that integer's floor-mod residue for every modulus,
+// written as int8 planes [n_mod][rows][res_ld] with K contiguous (the layout
+// the GEMM's TMA loads want).
+//
+// Two kernels cover the operand layouts:
+//   split_rows_kernel    K is the contiguous axis (A row-major, or B given as
+//                        the transpose of a row-major W): 128-bit loads along K,
+//                        a warp/CTA max-reduction, then residues.
+//   split_strided_*      K is strided (B row-major [K,N]): a column-max pass
+//                        with coalesced loads along N, then a tiled pass that
+//                        transposes through shared memory.
+#pragma once
+
+#include "fpemu_device.cuh"
+
+namespace fpemu {
+
+// frexp exponent of max(m, 1e-300) from the bit pattern of m = max|x| (ozaki.py:34-35).
+__device__ __forceinline__ int exp_from_maxbits(uint64_t mb) {
+    if (mb >= 0x7FF0000000000000ull) return kNonFiniteExp;  // Inf or NaN in the row
+    double m = __longlong_as_double((long long)mb);
+    if (m < 1e-300) m = 1e-300;
+    return (int)((__double_as_longlong(m) >> 52) & 0x7FF) - 1022;
+}
+
+// 2^t for t in [-1022, 1023], built from its bit pattern.
+__device__ __forceinline__ double pow2(int t) {
+    return __longlong_as_double((long long)(t + 1023) << 52);
+}
+
+// Scaled integer round_half_even(x * 2^s) for s in [-1024+bits, 1049] (exact: two
+// power-of-two products, then the int64 conversion rounds to nearest even).  A
+// product that underflows is below 2^-400 and rounds to 0 either way.
+__device__ __forceinline__ long long scale_round(double x, double f1, double f2) {
+    return __double2ll_rn(__dmul_rn(__dmul_rn(x, f1), f2));
+}
+
+// The 53-bit magnitude u of v split as u = a*2^36 + b*2^18 + c.  Then
+// u mod p == (a*(2^36 mod p) + b*(2^18 mod p) + c) mod p, and that folded sum
+// is below p*2^19; a negative v is folded to p*2^24 - t (same class as -u).
+struct Folded {
+    uint32_t a, b, c;
+    bool neg;
+};
+
+__device__ __forceinline__ Folded fold(long long v) {
+    const unsigned long long u = v < 0 ? (unsigned long long)(-v) : (unsigned long long)v;
+    Folded f;
+    f.a = (uint32_t)(u >> 36);
+    f.b = (uint32_t)(u >> 18) & 0x3FFFFu;
+    f.c = (uint32_t)u & 0x3FFFFu;
+    f.neg = v < 0;
+    return f;
+}
+
+__device__ __forceinline__ uint32_t residue_of(const Folded& f, const ModConsts& mc, int l) {
+    uint32_t t = f.a * mc.c36[l] + f.b * mc.c18[l] + f.c;
+    t = f.neg ? mc.kneg[l] - t : t;
+    return mod_small(t, mc.p[l], mc.magic[l], mc.shift[l]);
+}
+
+// Residues of 16 consecutive elements for every modulus, stored as one 16-byte
+// vector per plane.  `dst` is plane 0 of the chunk; planes are res_plane apart.
+__device__ __forceinline__ void store_chunk_residues(const long long (&v)[16], int n_mod,
+                                                     const ModConsts& mc, int8_t* dst,
+                                                     int64_t res_plane) {
+    Folded f[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) f[j] = fold(v[j]);
+#pragma unroll 1
+    for (int l = 0; l < n_mod; ++l) {
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t r0 = residue_of(f[4 * q + 0], mc, l);
+            const uint32_t r1 = residue_of(f[4 * q + 1], mc, l);
+            const uint32_t r2 = residue_of(f[4 * q + 2], mc, l);
+            const uint32_t r3 = residue_of(f[4 * q + 3], mc, l);
+            w[q] = r0 | (r1 << 8) | (r2 << 16) | (r3 << 24);
+        }
+        *reinterpret_cast<uint4*>(dst + (int64_t)l * res_plane) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// K contiguous.  GROUP threads (a multiple of 32, dividing blockDim) own one
+// row; each thread walks chunks of 16 elements, stride GROUP chunks.
+// VEC: the row start is 16-byte aligned, so chunks load as 8 x 16 bytes.
+// ---------------------------------------------------------------------------
+template <int GROUP, bool VEC>
+__global__ void __launch_bounds__(256) split_rows_kernel(const __grid_constant__ SplitParams P) {
+    static_assert(GROUP % 32 == 0 && 256 % GROUP == 0, "bad group");
+    constexpr int kRowsPerCta = 256 / GROUP;
+    constexpr int kWarps = GROUP / 32;
+    __shared__ unsigned long long red[256 / 32];
+
+    const int g = threadIdx.x / GROUP;       // row slot in this CTA
+    const int gt = threadIdx.x % GROUP;      // thread within the row group
+    const int warp_in_group = gt / 32;
+    const int64_t nchunk_in = (P.k + 15) / 16;
+    const int64_t nchunk_out = P.res_ld / 16;
+
+    for (int64_t row0 = (int64_t)blockIdx.x * kRowsPerCta; row0 < P.rows;
+         row0 += (int64_t)gridDim.x * kRowsPerCta) {
+        const int64_t row = row0 + g;
+        const bool live = row < P.rows;
+        const double* x = P.X + (live ? row : 0) * P.s_row;
+
+        // Pass 1: max |x| as the bit pattern of the magnitude (monotone for
+        // non-negative doubles; NaN patterns sort above Inf).
+        unsigned long long mb = 0;
+        if (live) {
+            for (int64_t c = gt; c < nchunk_in; c += GROUP) {
+                const int64_t t0 = c * 16;
+                if (VEC && t0 + 16 <= P.k) {
+                    const double2* p2 = reinterpret_cast<const double2*>(x + t0);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const double2 d = __ldg(p2 + j);
+                        mb = max(mb, (unsigned long long)__double_as_longlong(d.x) & 0x7FFFFFFFFFFFFFFFull);
+                        mb = max(mb, (unsigned long long)__double_as_longlong(d.y) & 0x7FFFFFFFFFFFFFFFull);
+                    }
+                } else {
+                    for (int j = 0; j < 16 && t0 + j < P.k; ++j) {
+                        const double d = __ldg(x + t0 + j);
+                        mb = max(mb, (unsigned long long)__double_as_longlong(d) & 0x7FFFFFFFFFFFFFFFull);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+        if (kWarps > 1) {
+            if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = mb;
+            __syncthreads();
+            mb = 0;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) mb = max(mb, red[g * kWarps + w]);
+            __syncthreads();
+        }
+        (void)warp_in_group;
+        if (!live) continue;
+
+        const int e = exp_from_maxbits(mb);
+        if (gt == 0) P.exps[row] = e;
+        const bool finite = e != kNonFiniteExp;
+        const int s = P.bits - e;
+        const double f1 = pow2(s >> 1), f2 = pow2(s - (s >> 1));
+
+        // Pass 2: the row again (from L1/L2), residues for every modulus.
+        int8_t* out_row = P.res + row * P.res_ld;
+        for (int64_t c = gt; c < nchunk_out; c += GROUP) {
+            const int64_t t0 = c * 16;
+            long long v[16];
+            if (finite && VEC && t0 + 16 <= P.k) {
+                const double2* p2 = reinterpret_cast<const double2*>(x + t0);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const double2 d = __ldg(p2 + j);
+                    v[2 * j] = scale_round(d.x, f1, f2);
+                    v[2 * j + 1] = scale_round(d.y, f1, f2);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    v[j] = (finite && t0 + j < P.k) ? scale_round(__ldg(x + t0 + j), f1, f2) : 0;
+            }
+            store_chunk_residues(v, P.n_mod, P.mc, out_row + t0, P.res_plane);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// K strided.  Pass 1: colmax[r] = max over t of |X[r, t]| (as bit patterns),
+// threads along r (coalesced when s_row == 1), blocks along t; colmax must be
+// zeroed first.
+// ---------------------------------------------------------------------------
+constexpr int kColmaxK = 256;
+
+__global__ void __launch_bounds__(256) split_colmax_kernel(const __grid_constant__ SplitParams P,
+                                                           unsigned long long* colmax) {
+    const int64_t r = (int64_t)blockIdx.x * 256 + threadIdx.x;
+    if (r >= P.rows) return;
+    const int64_t t0 = (int64_t)blockIdx.y * kColmaxK;
+    const int64_t t1 = min(t0 + (int64_t)kColmaxK, P.k);
+    unsigned long long mb = 0;
+    const double* x = P.X + r * P.s_row;
+    for (int64_t t = t0; t < t1; ++t)
+        mb = max(mb, (unsigned long long)__double_as_longlong(__ldg(x + t * P.s_k)) & 0x7FFFFFFFFFFFFFFFull);
+    atomicMax(colmax + r, mb);
+}
+
+// Pass 2: a CTA takes 32 rows x 128 k, loads them through shared memory
+// (coalesced along r), then each thread emits 16 consecutive k of one row.
+constexpr int kTileR = 32;
+constexpr int kTileK = 128;
+
+__global__ void __launch_bounds__(256) split_strided_kernel(const __grid_constant__ SplitParams P) {
+    // Element (t, r) sits at tile[t][r ^ swz(t)], swz(t) = 4 * ((t / 16) % 8), so the
+    // compute phase (8 k-chunks x 4 rows per warp) hits every bank pair once per
+    // wavefront, and the load phase (32 rows of one t) writes a permutation.
+    __shared__ double tile[kTileK][kTileR];
+    const int64_t r0 = (int64_t)blockIdx.x * kTileR;
+    const int64_t k0 = (int64_t)blockIdx.y * kTileK;
+
+    // Load: thread (tr = tid % 32, tk = tid / 32) reads rows r0+tr, k = k0+tk+8i.
+    {
+        const int tr = threadIdx.x % kTileR;
+        const int tk = threadIdx.x / kTileR;
+        const int64_t r = r0 + tr;
+#pragma unroll 4
+        for (int i = 0; i < kTileK / 8; ++i) {
+            const int64_t t = k0 + tk + 8 * i;
+            const int lt = tk + 8 * i;
+            tile[lt][tr ^ (((lt >> 4) & 7) << 2)] =
+                (r < P.rows && t < P.k) ? __ldg(P.X + r * P.s_row + t * P.s_k) : 0.0;
+        }
+    }
+    __syncthreads();
+
+    // Compute: thread (r = tid / 8, kc = tid % 8) handles k0 + 16*kc .. +16 of row r0 + r.
+    const int lr = threadIdx.x / 8;
+    const int kc = threadIdx.x % 8;
+    const int64_t row = r0 + lr;
+    const int64_t t0 = k0 + 16 * kc;
+    if (row >= P.rows || t0 >= P.res_ld) return;
+    const int e = exp_from_maxbits(P.colmax[row]);
+    if (blockIdx.y == 0 && kc == 0) P.exps[row] = e;
+    const bool finite = e != kNonFiniteExp;
+    const int s = P.bits - e;
+    const double f1 = pow2(s >> 1), f2 = pow2(s - (s >> 1));
+    long long v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+        v[j] = (finite && t0 + j < P.k) ? scale_round(tile[16 * kc + j][lr ^ ((kc & 7) << 2)], f1, f2) : 0;
+    store_chunk_residues(v, P.n_mod, P.mc, P.res + row * P.res_ld + t0, P.res_plane);
+}
+
+}  // namespace fpemu

@@ -1,0 +1,229 @@
+"""Ozaki scheme II on INT8 tensor cores -- the drop-in for the reference's
+``fp_emulation/ozaki.py`` (thezettascale/fp-emulation), backed by libfpemu.so.
+
+Same public function, same autograd behaviour, same exceptions as
+ozaki.py:95-145.  What changed is underneath: one split kernel per operand,
+one persistent tcgen05 GEMM whose epilogue reduces every accumulator modulo its
+prime and reconstructs FP64 C, all on the caller's current CUDA stream.  CUDA
+tensors only: there is no CPU path.
+
+The stage functions (``_split``, ``_matmul_residues``, ``_reconstruct``) keep
+the reference's step boundaries so each step can be compared with the
+reference on its own; the production call goes through one C entry point.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from fp_emulation import _lib
+
+# ozaki.py:6-9
+_PRIMES = [
+    3, 5, 7, 11, 13, 17, 19, 23, 29, 31, 37, 41, 43, 47, 53,
+    59, 61, 67, 71, 73, 79, 83, 89, 97, 101, 103, 107, 109, 113, 127,
+]
+
+# ozaki.py:12-17
+_PRECISION_BITS = {
+    torch.float16: 11,
+    torch.bfloat16: 8,
+    torch.float32: 24,
+    torch.float64: 53,
+}
+
+_CHECK = os.environ.get("FPEMU_CHECK", "0") not in ("", "0")
+
+
+def _n_moduli(k, bits):
+    """ozaki.py:20-29 through fpemu_plan_moduli; ValueError when the primes run out."""
+    n = ctypes.c_int(0)
+    _lib.check(_lib.load().fpemu_plan_moduli(int(k), int(bits), ctypes.byref(n), None), "_n_moduli")
+    return n.value
+
+
+def _crt_weights(moduli):
+    """ozaki.py:62-80 through fpemu_crt_weights (exact 128-bit integer arithmetic).
+    ``moduli`` must be a prefix of ``_PRIMES``, as the reference always uses."""
+    n = len(moduli)
+    if list(moduli) != _PRIMES[:n]:
+        raise ValueError("moduli must be the leading primes 3, 5, 7, ...")
+    arrs = [(ctypes.c_double * n)() for _ in range(3)]
+    scal = [ctypes.c_double() for _ in range(3)]
+    _lib.check(_lib.load().fpemu_crt_weights(n, *arrs, *[ctypes.byref(s) for s in scal]), "_crt_weights")
+    return list(arrs[0]), list(arrs[1]), list(arrs[2]), scal[0].value, scal[1].value, scal[2].value
+
+
+def _stream(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(*tensors):
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError(
+                "fp_emulation (B200 build) runs on CUDA tensors only; got a tensor on "
+                f"{t.device}. Move the operands to a CUDA device.")
+    dev = tensors[0].device
+    for t in tensors[1:]:
+        if t.device != dev:
+            raise RuntimeError(f"operands on different devices: {dev} and {t.device}")
+    return dev
+
+
+def _res_ld(k: int) -> int:
+    return ((k + 15) // 16) * 16
+
+
+def _after_call(what: str) -> None:
+    """With FPEMU_CHECK=1, synchronise and surface any device-side failure."""
+    if _CHECK:
+        code, where, block, detail = _lib.device_error(clear=True)
+        if code:
+            raise _lib.FpemuError(code, f"{what}: device wait timed out (where={where} block={block} "
+                                        f"detail={detail})")
+
+
+# ------------------------------------------------------------------ stages --
+
+def _split(X, bits, n_mod):
+    """ozaki.py:32-46 for one operand, fused on the GPU: returns
+    (residues int8 [n_mod, rows, res_ld] with K contiguous, exps int32 [rows]).
+
+    ``X`` is [rows, k]; for the reference's B [k, n] pass ``B.T``.  Residues
+    equal ``(round(ldexp(X, bits - exp)) mod p)`` in [0, p); the columns past k
+    are zero.
+    """
+    dev = _require_cuda(X)
+    X = X.double()
+    rows, k = X.shape
+    ld = _res_ld(k)
+    res = torch.empty((n_mod, rows, ld), dtype=torch.int8, device=dev)
+    exps = torch.empty((rows,), dtype=torch.int32, device=dev)
+    colmax = torch.empty((max(rows, 1),), dtype=torch.int64, device=dev) if X.stride(1) != 1 else None
+    with torch.cuda.device(dev):
+        st = _lib.load().fpemu_split(rows, k, X.data_ptr(), X.stride(0), X.stride(1), bits, n_mod,
+                                     res.data_ptr(), ld, rows * ld, exps.data_ptr(),
+                                     None if colmax is None else colmax.data_ptr(), _stream(dev))
+    _lib.check(st, "_split")
+    _after_call("_split")
+    return res, exps
+
+
+def _scale_to_int_residues(A, B, bits, n_mod):
+    """The reference's _scale_to_int + _residues for both operands (ozaki.py:111-113)."""
+    a_res, row_exp = _split(A, bits, n_mod)
+    b_res, col_exp = _split(B.T, bits, n_mod)
+    return a_res, b_res, row_exp, col_exp
+
+
+def _matmul_residues(a_res, b_res, moduli, raw=False):
+    """ozaki.py:49-59: per-modulus products of the K-major residue planes.
+    ``raw=False`` gives (a_l @ b_l^T) mod p_l as uint8 [n_mod, m, n] (the
+    reference returns the same values as int32); ``raw=True`` gives the int32
+    products before the reduction."""
+    dev = _require_cuda(a_res, b_res)
+    n_mod, m, ld = a_res.shape
+    n = b_res.shape[1]
+    k = ld  # zero columns past the true k contribute nothing
+    out = torch.empty((n_mod, m, n), dtype=torch.int32 if raw else torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        st = _lib.load().fpemu_gemm_residues(m, n, k, n_mod, a_res.data_ptr(), b_res.data_ptr(), ld,
+                                             0 if raw else 1, out.data_ptr(), None, 0, _stream(dev))
+    _lib.check(st, "_matmul_residues")
+    _after_call("_matmul_residues")
+    return out
+
+
+def _reconstruct(residues, moduli, bits, row_exp, col_exp):
+    """ozaki.py:83-92: CRT reconstruction from uint8 residues [n_mod, m, n]."""
+    dev = _require_cuda(residues, row_exp, col_exp)
+    res = residues.to(torch.uint8).contiguous()
+    n_mod, m, n = res.shape
+    out = torch.empty((m, n), dtype=torch.float64, device=dev)
+    re = row_exp.to(torch.int32).contiguous()
+    ce = col_exp.to(torch.int32).contiguous()
+    with torch.cuda.device(dev):
+        st = _lib.load().fpemu_crt_reconstruct(m, n, n_mod, res.data_ptr(), re.data_ptr(), ce.data_ptr(),
+                                               bits, out.data_ptr(), n, _stream(dev))
+    _lib.check(st, "_reconstruct")
+    _after_call("_reconstruct")
+    return out
+
+
+# --------------------------------------------------------------- forward ----
+
+def _workspace(m, n, k, n_mod, dev):
+    nbytes = _lib.load().fpemu_workspace_size(m, n, k, n_mod)
+    if nbytes == 0:
+        raise _lib.FpemuError(_lib.FPEMU_ERR_NO_DEVICE, "fpemu_workspace_size failed: "
+                              + _lib.load().fpemu_last_error().decode(errors="replace"))
+    return torch.empty((nbytes,), dtype=torch.uint8, device=dev)
+
+
+def _ozaki2_forward(A, B, n_mod=None):
+    """ozaki.py:95-119: scale -> modular INT8 matmuls -> CRT reconstruct, as one
+    C call (split A, split B, fused GEMM + CRT) on the current stream.
+    ``n_mod`` overrides the reference's modulus count (for sweeps)."""
+    bits = _PRECISION_BITS.get(A.dtype)
+    if bits is None:
+        supported = ", ".join(str(d) for d in _PRECISION_BITS)
+        raise TypeError(
+            f"unsupported dtype {A.dtype}. "
+            f"CRT matmul emulates floating-point precision via int8 arithmetic; "
+            f"input must be a float type ({supported})"
+        )
+    dev = _require_cuda(A, B)
+    if A.dim() != 2 or B.dim() != 2 or A.shape[1] != B.shape[0]:
+        raise RuntimeError(f"ozaki2_int8_matmul: expected [m,k] @ [k,n], got {tuple(A.shape)} @ {tuple(B.shape)}")
+    orig_dtype = A.dtype
+    A, B = A.double(), B.double()
+    m, k = A.shape
+    n = B.shape[1]
+    if k == 0:
+        raise RuntimeError("ozaki2_int8_matmul: inner dimension k must be non-zero "
+                           "(the reference's amax over an empty dimension fails the same way)")
+    if n_mod is None:
+        n_mod = _n_moduli(k, bits)
+    C = torch.empty((m, n), dtype=torch.float64, device=dev)
+    if m and n:
+        with torch.cuda.device(dev):
+            ws = _workspace(m, n, k, n_mod, dev)
+            st = _lib.load().fpemu_ozaki2_dgemm(
+                m, n, k, A.data_ptr(), A.stride(0), A.stride(1), B.data_ptr(), B.stride(0), B.stride(1),
+                C.data_ptr(), n, bits, n_mod, ws.data_ptr(), ws.numel(), _stream(dev))
+        _lib.check(st, "ozaki2_int8_matmul")
+        _after_call("ozaki2_int8_matmul")
+    if orig_dtype != torch.float64:
+        C = C.to(orig_dtype)
+    return C
+
+
+class _OzakiMatmul(torch.autograd.Function):
+    """ozaki.py:122-136: backward re-enters the emulated product twice."""
+
+    @staticmethod
+    def forward(A, B):
+        return _ozaki2_forward(A, B)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        ctx.save_for_backward(*inputs)
+
+    @staticmethod
+    def backward(ctx, grad):
+        A, B = ctx.saved_tensors
+        grad_A = ozaki2_int8_matmul(grad, B.T) if ctx.needs_input_grad[0] else None
+        grad_B = ozaki2_int8_matmul(A.T, grad) if ctx.needs_input_grad[1] else None
+        return grad_A, grad_B
+
+
+def ozaki2_int8_matmul(A, B):
+    """
+    FP-accurate matmul via INT8 tensor cores (Ozaki scheme II + CRT).
+
+    Precision matches input dtype (fp16, bf16, fp32, fp64).  CUDA tensors only.
+    """
+    return _OzakiMatmul.apply(A, B)

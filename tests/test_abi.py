@@ -1,0 +1,128 @@
+"""C-ABI and host-logic tests that need no GPU.
+
+* libfpemu.so loads and exports every symbol include/fpemu.h declares;
+* its host-side planning (moduli, CRT weights, int32 limit) equals the oracle;
+* the integer tricks the kernels rely on (magic-number division, the 3-limb
+  fold of 53-bit integers) are exact, checked here over their input ranges;
+* the Python layer raises the reference's exceptions before touching a GPU.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+
+import numpy as np
+import pytest
+
+from conftest import REPO
+from oracle import ozaki_oracle as oo
+
+HEADER = REPO / "include" / "fpemu.h"
+
+
+def _lib():
+    from fp_emulation import _lib as L
+
+    return L.load()
+
+
+def test_library_exports_every_declared_symbol():
+    names = set(re.findall(r"\b(fpemu_[a-z0-9_]+)\s*\(", HEADER.read_text()))
+    assert len(names) >= 14
+    lib = _lib()
+    for name in sorted(names):
+        assert hasattr(lib, name), name
+    from fp_emulation import _lib as L
+
+    assert names == set(L.SIGNATURES), "ctypes signatures out of sync with the header"
+    assert lib.fpemu_abi_version() == 1
+
+
+@pytest.mark.parametrize("bits", [53, 24, 11, 8])
+def test_plan_moduli_matches_reference_rule(bits):
+    lib = _lib()
+    n = ctypes.c_int()
+    mods = (ctypes.c_int32 * 32)()
+    for k in [1, 2, 16, 20, 255, 256, 1000, 4096, 4097, 8191, 8192, 16384, 131072, 214748]:
+        assert lib.fpemu_plan_moduli(k, bits, ctypes.byref(n), mods) == 0
+        assert n.value == oo.n_moduli(k, bits), (k, bits)
+        assert list(mods[: n.value]) == oo.PRIMES[: n.value]
+    assert lib.fpemu_plan_moduli(2 ** 60, 53, ctypes.byref(n), None) == 2  # FPEMU_ERR_NO_MODULI
+
+
+def test_crt_weights_bit_identical_to_reference_formula():
+    lib = _lib()
+    for n_mod in range(1, 26):
+        arr = [(ctypes.c_double * n_mod)() for _ in range(3)]
+        sc = [ctypes.c_double() for _ in range(3)]
+        assert lib.fpemu_crt_weights(n_mod, *arr, *[ctypes.byref(s) for s in sc]) == 0
+        ref = oo.crt_weights(oo.PRIMES[:n_mod])
+        for got, want in zip(arr, ref[:3]):
+            np.testing.assert_array_equal(np.array(list(got)).view(np.int64), np.array(want).view(np.int64))
+        for got, want in zip(sc, ref[3:]):
+            assert np.float64(got.value).view(np.int64) == np.float64(want).view(np.int64)
+    assert lib.fpemu_crt_weights(26, *arr, *[ctypes.byref(s) for s in sc]) == 3  # FPEMU_ERR_UNSUPPORTED
+
+
+def test_max_k_is_the_int32_limit():
+    lib = _lib()
+    assert lib.fpemu_max_k(25) == (2 ** 31 - 1) // (100 * 100)
+    assert lib.fpemu_max_k(24) == (2 ** 31 - 1) // (96 * 96)
+
+
+def _mod_consts(p):
+    s = p.bit_length() - 1
+    return s, -(-(1 << (32 + s)) // p)
+
+
+def test_magic_division_exact_below_2_31():
+    """floor(n/p) == (n * magic) >> (32 + s) for every n < 2^31 (checked on a dense
+    set: every multiple-of-p boundary neighbourhood plus random values)."""
+    rng = np.random.default_rng(0)
+    for p in oo.PRIMES[:25]:
+        s, magic = _mod_consts(p)
+        assert magic < 2 ** 32
+        q = np.arange(0, (2 ** 31 - 1) // p + 1, max(1, ((2 ** 31) // p) // 200_000), dtype=np.uint64)
+        n = np.concatenate([q * p, q * p + p - 1, q * p + 1,
+                            rng.integers(0, 2 ** 31, 200_000, dtype=np.uint64),
+                            np.array([2 ** 31 - 1, 0, p - 1], dtype=np.uint64)])
+        n = n[n < 2 ** 31]
+        got = ((n * np.uint64(magic)) >> np.uint64(32)) >> np.uint64(s)
+        np.testing.assert_array_equal(got, n // np.uint64(p))
+
+
+def test_fold_residues_exact():
+    """The split kernel's residue path: |v| = a*2^36 + b*2^18 + c, fold with
+    2^36 mod p and 2^18 mod p, negate as p*2^24 - t, reduce by magic division;
+    must equal Python's floor-mod for |v| <= 2^53."""
+    rng = np.random.default_rng(1)
+    v = np.concatenate([rng.integers(-(2 ** 53), 2 ** 53 + 1, 300_000, dtype=np.int64),
+                        np.array([0, 1, -1, 2 ** 53, -(2 ** 53), 2 ** 53 - 1, -(2 ** 36), 2 ** 18 - 1],
+                                 dtype=np.int64)])
+    u = np.abs(v).astype(np.uint64)
+    a, b, c = u >> np.uint64(36), (u >> np.uint64(18)) & np.uint64(0x3FFFF), u & np.uint64(0x3FFFF)
+    for p in oo.PRIMES[:25]:
+        s, magic = _mod_consts(p)
+        t = a * np.uint64((1 << 36) % p) + b * np.uint64((1 << 18) % p) + c
+        assert int(t.max()) < p << 24
+        t = np.where(v < 0, np.uint64(p << 24) - t, t)
+        assert int(t.max()) < 2 ** 31
+        r = t - (((t * np.uint64(magic)) >> np.uint64(32 + s)) * np.uint64(p))
+        np.testing.assert_array_equal(r.astype(np.int64), np.mod(v, p))
+
+
+def test_python_layer_errors_without_gpu():
+    import torch
+
+    from fp_emulation import ozaki2_int8_matmul
+    from fp_emulation.ozaki import _crt_weights, _n_moduli
+
+    assert _n_moduli(16384, 53) == 25
+    assert _crt_weights(oo.PRIMES[:24]) == tuple(oo.crt_weights(oo.PRIMES[:24])) or \
+        list(_crt_weights(oo.PRIMES[:24])) == list(oo.crt_weights(oo.PRIMES[:24]))
+    with pytest.raises(ValueError):
+        _n_moduli(2 ** 60, 53)
+    with pytest.raises(TypeError):  # ozaki.py:99-104: dtype first
+        ozaki2_int8_matmul(torch.ones(2, 2, dtype=torch.int32), torch.ones(2, 2, dtype=torch.int32))
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        ozaki2_int8_matmul(torch.ones(2, 2, dtype=torch.float64), torch.ones(2, 2, dtype=torch.float64))
