@@ -1,0 +1,472 @@
+#!/usr/bin/env python
+"""Benchmark: emulated FP64 TFLOPS (2mnk/t) of Ozaki scheme II at n = 16384.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (BASELINE.json config 2 at its n = 16384 point): square FP64 A, B with
+entries (U(0,1) - 0.5) * exp(phi * N(0,1)), phi = 1, seeded synthetic data,
+n_mod = 25 (the reference's choice for k = 16384).  A step is one full
+emulated product: split A, split B, fused INT8 GEMM + mod + CRT.  Operands are
+2 GiB each (larger than L2), so no flush is needed between steps.
+
+With N > 1 (torchrun, one rank per GPU, NCCL) A is row-sharded over the ranks
+and B's residues are broadcast from rank 0; the job is the same n = 16384
+product (strong scaling).
+
+`value` times the step on resident inputs (CUDA events, max over ranks);
+`e2e` times the public op with the operands copied from pinned host memory
+and C copied back inside the timed region.  Rank 0 prints one JSON line.
+
+`--impl reference` times the reference's own CPU path (its torch op sequence
+and its compiled crt_reconstruct.cpp) on the host cores, one bounded block of
+the same product per step, extrapolated to the full product.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (str(REPO / "fp-emulation_b200"), str(REPO)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "emulated FP64 TFLOPS (2mnk/t) at n=16384, 1/2/4/8 B200; INT8 TC util %"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--n", type=int, default=16384)
+    ap.add_argument("--phi", type=float, default=1.0)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-extras", action="store_true", help="skip DGEMM/cuBLASLt/CPU side numbers")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) leg")
+    return ap.parse_args()
+
+
+def workload_config(n, phi, n_mod, world):
+    return {
+        "workload": f"BASELINE config 2 point n={n}: square FP64 GEMM, entries (U(0,1)-0.5)*exp({phi}*N(0,1))",
+        "m": n, "n": n, "k": n, "n_mod": n_mod, "phi": phi,
+        "l2": "inputs larger than L2 (2 GiB per operand); no flush",
+        "parallelism": "single GPU" if world == 1 else f"A row-sharded over {world} GPUs, B residues NCCL-broadcast",
+    }
+
+
+# ---------------------------------------------------------------- clocks ----
+
+class ClockSampler:
+    """nvidia-smi samples of one GPU (by UUID) while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.uuid}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, mx, reasons = [], None, set()
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[3:7]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------- helpers -----
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def measured_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            pass
+    return {}
+
+
+def gemm_traffic_per_launch(n):
+    """Per-launch DRAM traffic of the GEMM kernel from the committed ncu summary."""
+    p = REPO / "profiles" / "gemm_crt_traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return d.get(str(n))
+    except Exception:
+        return None
+
+
+def synth(torch, rows, cols, phi, seed, device):
+    g = torch.Generator(device=device).manual_seed(seed)
+    u = torch.rand(rows, cols, dtype=torch.float64, generator=g, device=device)
+    e = torch.randn(rows, cols, dtype=torch.float64, generator=g, device=device)
+    return (u - 0.5) * torch.exp(phi * e)
+
+
+# ---------------------------------------------------------------- ours -----
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from fp_emulation import _lib
+    from fp_emulation.distributed import ozaki2_int8_matmul_rowsharded, shard_rows
+    from fp_emulation.ozaki import _n_moduli, _res_ld, ozaki2_int8_matmul
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    lib = _lib.load()
+    n, k = args.n, args.n
+    r0, r1 = shard_rows(n, world, rank)
+    m = r1 - r0
+    bits = 53
+    n_mod = _n_moduli(k, bits)
+    ld = _res_ld(k)
+    root = 0
+
+    A = synth(torch, m, k, args.phi, args.seed + 1 + rank, dev)
+    B = synth(torch, k, n, args.phi, args.seed + 1000, dev) if rank == root else None
+
+    a_res = torch.empty((n_mod, m, ld), dtype=torch.int8, device=dev)
+    b_res = torch.empty((n_mod, n, ld), dtype=torch.int8, device=dev)
+    re = torch.empty((m,), dtype=torch.int32, device=dev)
+    ce = torch.empty((n,), dtype=torch.int32, device=dev)
+    colmax = torch.empty((n,), dtype=torch.int64, device=dev)
+    C = torch.empty((m, n), dtype=torch.float64, device=dev)
+    ws_bytes = lib.fpemu_gemm_workspace_size(m, n, n_mod)
+    ws = torch.empty((max(ws_bytes, 256),), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+
+    n_steps_events = []
+
+    def step(record):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
+        if ev: ev[0].record(stream)
+        _lib.check(lib.fpemu_split(m, k, A.data_ptr(), A.stride(0), A.stride(1), bits, n_mod, a_res.data_ptr(),
+                                   ld, m * ld, re.data_ptr(), None, sp), "split A")
+        if ev: ev[1].record(stream)
+        if rank == root:
+            _lib.check(lib.fpemu_split(n, k, B.data_ptr(), B.stride(1), B.stride(0), bits, n_mod,
+                                       b_res.data_ptr(), ld, n * ld, ce.data_ptr(), colmax.data_ptr(), sp),
+                       "split B")
+        if world > 1:
+            dist.broadcast(b_res, src=root)
+            dist.broadcast(ce, src=root)
+        if ev: ev[2].record(stream)
+        _lib.check(lib.fpemu_gemm_crt(m, n, k, n_mod, a_res.data_ptr(), b_res.data_ptr(), ld, re.data_ptr(),
+                                      ce.data_ptr(), bits, C.data_ptr(), n, ws.data_ptr(), ws.numel(), sp),
+                   "gemm_crt")
+        if ev:
+            ev[3].record(stream)
+            n_steps_events.append(ev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    def sum_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return t.item()
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize(dev)
+    code = _lib.device_error(clear=True)
+    if code[0]:
+        raise RuntimeError(f"device-side failure during warm-up: {code}")
+
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(uuid) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            step(True)
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    elapsed_ms = max_over_ranks(start.elapsed_time(end))
+    code = _lib.device_error(clear=True)
+    if code[0]:
+        raise RuntimeError(f"device-side failure in the timed region: {code}")
+    ms_step = elapsed_ms / args.steps
+    flops = 2.0 * n * n * k
+    value = flops / (ms_step * 1e-3) / 1e12
+
+    split_a_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in n_steps_events)
+    split_b_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in n_steps_events)
+    gemm_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in n_steps_events)
+    int8_ops = 2.0 * m * n * k * n_mod
+    achieved = int8_ops / (gemm_ms * 1e-3) / 1e12
+    peaks = measured_peaks()
+    if peaks.get("bf16_tflops_sustained"):
+        peak, peak_src = 2.0 * peaks["bf16_tflops_sustained"], "2 x bf16_tflops_sustained of measured (INT8 dense = 2 x BF16 dense)"
+    else:
+        peak, peak_src = 2.0 * 1590.0, "2 x 1.59 PFLOP/s bf16 of fallback"
+    # Our kernels per step: split A (1), split B on the root (column max + split: 2), GEMM (1).
+    launches = int(sum_over_ranks((1 + (2 if rank == root else 0) + 1) * args.steps))
+
+    # ---- end to end through the public op, host buffers ------------------
+    e2e = None
+    if not args.no_e2e:
+        A_h = A.cpu().pin_memory()
+        B_h = B.cpu().pin_memory() if rank == root else None
+        C_h = torch.empty((m, n), dtype=torch.float64).pin_memory()
+        A_d = torch.empty_like(A)
+        B_d = torch.empty((k, n), dtype=torch.float64, device=dev) if rank == root else None
+        del a_res  # give the public op's own workspace room
+
+        def e2e_step():
+            A_d.copy_(A_h, non_blocking=True)
+            if rank == root:
+                B_d.copy_(B_h, non_blocking=True)
+            if world == 1:
+                Cd = ozaki2_int8_matmul(A_d, B_d)
+            else:
+                Cd = ozaki2_int8_matmul_rowsharded(A_d, B_d, n=n, root=root)
+            C_h.copy_(Cd, non_blocking=True)
+
+        e2e_steps = max(2, args.steps // 2)
+        for _ in range(max(1, args.warmup - 1)):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        barrier()
+        s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        t2.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        e2e_ms = max_over_ranks(s2.elapsed_time(t2)) / e2e_steps
+        h2d = sum_over_ranks(A_h.numel() * 8 + (B_h.numel() * 8 if B_h is not None else 0))
+        d2h = sum_over_ranks(C_h.numel() * 8)
+        e2e = {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 3)}
+        # Sanity guard on the last end-to-end result: a row sample against cuBLAS DGEMM.
+        if world == 1:
+            rows = torch.arange(0, m, max(1, m // 64))
+            ref_rows = (A_d[rows.to(dev)] @ B_d).cpu()
+            got_rows = C_h[rows]
+            rel = ((got_rows - ref_rows).abs().max() / ref_rows.abs().max()).item()
+            if not rel < 1e-12:
+                raise RuntimeError(f"sanity check failed: max rel diff vs DGEMM {rel}")
+
+    extras = {}
+    if not args.no_extras:
+        extras = side_numbers(torch, dev, A, B if rank == root else None, b_res, m, n, k, n_mod, rank, root,
+                              world, args)
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8", "emulated": "f64", "data": "synthetic (seeded, generated on device)",
+            "config": workload_config(n, args.phi, n_mod, world),
+            "e2e": e2e,
+            "roofline": {"bound": "tensor", "kernel": "ozaki_gemm_kernel (fused INT8 GEMM + mod + CRT)",
+                         "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                         "ops_per_launch": int8_ops, "launch_ms": round(gemm_ms, 3),
+                         "traffic": gemm_traffic_per_launch(n)},
+            "int8_tc_util": round(achieved / peak, 4),
+            "stages_ms": {"split_a": round(split_a_ms, 3), "split_b": round(split_b_ms, 3),
+                          "gemm_crt": round(gemm_ms, 3)},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+        out.update(extras)
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def side_numbers(torch, dev, A, B, b_res, m, n, k, n_mod, rank, root, world, args):
+    """cuBLAS DGEMM and cuBLASLt INT8 on the same GPU, and the reference's CPU path
+    on this host's cores (rank 0, single GPU only)."""
+    out = {}
+    if rank == root:
+        Bm = B
+        for _ in range(2):
+            torch.matmul(A, Bm)
+        torch.cuda.synchronize(dev)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 3
+        s.record()
+        for _ in range(reps):
+            torch.matmul(A, Bm)
+        e.record()
+        torch.cuda.synchronize(dev)
+        dg_ms = s.elapsed_time(e) / reps
+        out["dgemm_cublas"] = {"tflops": round(2.0 * m * n * k / (dg_ms * 1e-3) / 1e12, 3), "ms": round(dg_ms, 3),
+                               "shape": [m, n, k]}
+        # cuBLASLt INT8 (the reference's GEMM backend) on one modulus plane, same shape.
+        try:
+            a8 = torch.randint(0, 101, (m, k), dtype=torch.int8, device=dev)
+            b8 = b_res[0][:, :k]
+            bT = b8.t()
+            for _ in range(2):
+                torch._int_mm(a8, bT)
+            torch.cuda.synchronize(dev)
+            s.record()
+            for _ in range(reps):
+                torch._int_mm(a8, bT)
+            e.record()
+            torch.cuda.synchronize(dev)
+            i8_ms = s.elapsed_time(e) / reps
+            i8 = 2.0 * m * n * k / (i8_ms * 1e-3) / 1e12
+            out["int8_cublaslt"] = {"tops_per_modulus_gemm": round(i8, 1), "ms": round(i8_ms, 3),
+                                    "effective_fp64_tflops_at_n_mod": round(i8 / n_mod, 3)}
+        except Exception as exc:  # torch._int_mm layout limits
+            out["int8_cublaslt"] = {"error": str(exc)[:200]}
+    if rank == 0 and world == 1:
+        out["cpu_baseline"] = cpu_baseline(args, torch)
+    return out
+
+
+def cpu_baseline(args, torch, r=256, c=256):
+    from oracle.reference_path import block_time, crt_kind, synthetic_block
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    n = args.n
+    A, B = synthetic_block(n, 32, 32, args.phi, args.seed)
+    block_time(A, B, n, n)  # warm-up (also loads the compiled CRT)
+    A, B = synthetic_block(n, r, c, args.phi, args.seed)
+    est, blk, st = block_time(A, B, n, n)
+    return {"value": round(2.0 * n ** 3 / est / 1e12, 9), "unit": "TFLOPS", "cores": cores,
+            "kind": crt_kind(),
+            "sample": f"{r}x{c} block of the n={n} product (full K), {blk:.1f} s wall; stages "
+                      f"split_a/split_b/int32-matmul/crt = {', '.join(f'{x:.2f}' for x in st)} s, "
+                      f"extrapolated to the full product ({est / 3600:.2f} h): reference torch op "
+                      f"sequence + crt_reconstruct.cpp compiled from the reference source"}
+
+
+# ---------------------------------------------------------------- reference arm ---
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if world > 1 and rank != 0:
+        return
+    import torch
+
+    from oracle.ozaki_oracle import n_moduli
+    from oracle.reference_path import block_time, crt_kind, synthetic_block
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    n = args.n
+    n_mod = n_moduli(n, 53)
+    r, c = 128, 256
+    A, B = synthetic_block(n, r, c, args.phi, args.seed)
+    for _ in range(args.warmup):
+        block_time(A[:16], B[:, :16], n, n)
+    ests, walls = [], []
+    for _ in range(args.steps):
+        est, blk, _ = block_time(A, B, n, n)
+        ests.append(est)
+        walls.append(blk)
+    est = statistics.mean(ests)
+    value = 2.0 * n ** 3 / est / 1e12
+    out = {
+        "metric": METRIC, "value": round(value, 9), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(est * 1e3, 1), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int32", "emulated": "f64",
+        "data": "synthetic (seeded)", "impl": "reference",
+        "config": workload_config(n, args.phi, n_mod, world),
+        "cpu_baseline": {"value": round(value, 9), "unit": "TFLOPS", "cores": cores, "kind": crt_kind(),
+                         "sample": f"per step one {r}x{c} block of the n={n} product (full K, "
+                                   f"{statistics.mean(walls):.1f} s wall) through the reference's CPU op "
+                                   f"sequence + its crt_reconstruct.cpp, extrapolated to the full product"},
+        "e2e": {"value": round(value, 9), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

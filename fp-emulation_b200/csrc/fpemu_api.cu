@@ -13,6 +13,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <algorithm>
 #include <string>
 
 #include "crt_kernels.cuh"
@@ -47,10 +48,13 @@ int fail(int code, const char* fmt, ...) {
         if (s_ != FPEMU_OK) return s_; \
     } while (0)
 
-// The GEMM configuration used by the fused path and the parity taps:
-// 128 x 256 tiles, 4-stage ring of 48 KB, 8 epilogue warps, 2 accumulators
-// (2 x 256 TMEM columns = all 512).
-using MainCfg = GemmCfg<256, 4, 8, 2>;
+// GEMM configurations.  Main: CTA pairs (2-SM MMA, M = 256) on 256 x 256
+// tiles, a 6-stage ring of 32 KB per CTA, 8 epilogue warps, 2 accumulators of
+// 256 TMEM columns.  Single: one CTA per 128 x 256 tile, 4 stages of 48 KB
+// (kept as an independent cross-check; FPEMU_GEMM_CTAS=1 selects it).
+using MainCfg = GemmCfg<2, 256, 6, 8, 2>;
+using SingleCfg = GemmCfg<1, 256, 4, 8, 2>;
+static_assert(MainCfg::BN == SingleCfg::BN, "both configurations share the workspace layout");
 
 struct DevInfo {
     int sms = 0;
@@ -223,13 +227,61 @@ int64_t max_k(int n_mod) {
 inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 inline int64_t res_ld_for(int64_t k) { return ((k + 15) / 16) * 16; }
 
-int gemm_grid(const DevInfo& d, int64_t m, int64_t n) {
-    const int64_t tiles = ((m + kBM - 1) / kBM) * ((n + MainCfg::BN - 1) / MainCfg::BN);
-    return (int)(tiles < d.sms ? tiles : d.sms);
+bool use_pairs() {
+    const char* s = getenv("FPEMU_GEMM_CTAS");
+    return !(s && atoi(s) == 1);
+}
+
+// Co-resident clusters of the pair kernel on this device (GPC shapes may leave
+// some SMs unpaired); the persistent grid must not exceed what runs at once.
+template <class Cfg, int MODE>
+int max_active_units(const DevInfo& d) {
+    auto kern = ozaki_gemm_kernel<Cfg, MODE>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) != cudaSuccess)
+        return 0;
+    if (Cfg::CG == 1) return d.sms;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * d.sms);
+    cfg.blockDim = dim3(Cfg::kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = Cfg::CG;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) return 0;
+    return clusters;
+}
+
+// Launch units (CTAs, or CTA pairs) for an m x n problem; cached per device.
+template <class Cfg>
+int gemm_units(const DevInfo& d, int64_t m, int64_t n) {
+    static std::mutex mu;
+    static int cache[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int cap;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (cache[dev & 63] == 0) cache[dev & 63] = max_active_units<Cfg, kModeCrt>(d);
+        cap = cache[dev & 63];
+    }
+    const int64_t tiles = ((m + Cfg::kTileM - 1) / Cfg::kTileM) * ((n + Cfg::BN - 1) / Cfg::BN);
+    return (int)(tiles < cap ? tiles : cap);
+}
+
+int gemm_ctas(const DevInfo& d, int64_t m, int64_t n) {
+    return use_pairs() ? 2 * gemm_units<MainCfg>(d, m, n) : gemm_units<SingleCfg>(d, m, n);
 }
 
 size_t gemm_scratch_bytes(const DevInfo& d, int64_t m, int64_t n, int n_mod) {
-    return align256((size_t)gemm_grid(d, m, n) * (size_t)MainCfg::scratch_per_cta(n_mod));
+    // Per CTA the staging is the same for both configurations (128 x 256 outputs).
+    const int64_t ctas = std::max(2 * (int64_t)gemm_units<MainCfg>(d, m, n), (int64_t)gemm_units<SingleCfg>(d, m, n));
+    return align256((size_t)ctas * (size_t)MainCfg::scratch_per_cta(n_mod));
 }
 
 struct Layout {
@@ -289,27 +341,46 @@ int launch_split(const SplitParams& P, uint64_t* colmax, const DevInfo& d, cudaS
     return FPEMU_OK;
 }
 
-template <int MODE>
-int launch_gemm(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int64_t res_ld, const DevInfo& d,
-                cudaStream_t st) {
+template <class Cfg, int MODE>
+int launch_gemm_cfg(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int64_t res_ld, const DevInfo& d,
+                    cudaStream_t st) {
     const int64_t m = P.m, n = P.n;
-    if (m == 0 || n == 0) return FPEMU_OK;
     const int64_t res_plane_a = m * res_ld, res_plane_b = n * res_ld;
     CUtensorMap ta, tb;
     FPEMU_TRY(make_residue_map(&ta, a_res, P.k, m, P.n_mod, res_ld, res_plane_a, kBM));
-    FPEMU_TRY(make_residue_map(&tb, b_res, P.k, n, P.n_mod, res_ld, res_plane_b, MainCfg::BN));
+    FPEMU_TRY(make_residue_map(&tb, b_res, P.k, n, P.n_mod, res_ld, res_plane_b, Cfg::kBRows));
     P.num_kb = (int)((P.k + kBK - 1) / kBK);
-    P.tiles_m = (int)((m + kBM - 1) / kBM);
-    P.tiles_n = (int)((n + MainCfg::BN - 1) / MainCfg::BN);
+    P.tiles_m = (int)((m + Cfg::kTileM - 1) / Cfg::kTileM);
+    P.tiles_n = (int)((n + Cfg::BN - 1) / Cfg::BN);
     P.num_tiles = P.tiles_m * P.tiles_n;
     P.budget_ns = wait_budget_ns();
     mod_consts(P.n_mod, &P.mc);
-    const int grid = gemm_grid(d, m, n);
-    auto kern = ozaki_gemm_kernel<MainCfg, MODE>;
-    FPEMU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MainCfg::kSmemBytes));
-    kern<<<grid, MainCfg::kThreads, MainCfg::kSmemBytes, st>>>(ta, tb, P);
-    FPEMU_CUDA(cudaGetLastError());
+    const int units = gemm_units<Cfg>(d, m, n);
+    if (units < 1) return fail(FPEMU_ERR_CUDA, "GEMM kernel cannot be made resident on this device");
+    auto kern = ozaki_gemm_kernel<Cfg, MODE>;
+    FPEMU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(units * Cfg::CG));
+    cfg.blockDim = dim3(Cfg::kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = Cfg::CG;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = Cfg::CG > 1 ? 1 : 0;
+    FPEMU_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, P));
     return FPEMU_OK;
+}
+
+template <int MODE>
+int launch_gemm(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int64_t res_ld, const DevInfo& d,
+                cudaStream_t st) {
+    if (P.m == 0 || P.n == 0) return FPEMU_OK;
+    return use_pairs() ? launch_gemm_cfg<MainCfg, MODE>(P, a_res, b_res, res_ld, d, st)
+                       : launch_gemm_cfg<SingleCfg, MODE>(P, a_res, b_res, res_ld, d, st);
 }
 
 int check_gemm_args(int64_t m, int64_t n, int64_t k, int n_mod, const void* a_res, const void* b_res,

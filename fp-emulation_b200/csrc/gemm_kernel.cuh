@@ -36,11 +36,15 @@ constexpr int kBK = 128;       // K bytes per stage: one 128-byte swizzle row
 constexpr int kUmmaK = 32;     // K of one tcgen05.mma kind::i8
 constexpr int kBandRows = 16;  // tile rows per raster band (L2 reuse of A and B)
 
-template <int BN_, int STAGES_, int NEPI_, int NACC_>
+template <int CG_, int BN_, int STAGES_, int NEPI_, int NACC_>
 struct GemmCfg {
+    static constexpr int CG = CG_;  // CTAs per MMA: 1, or 2 (a cluster pair, M = 256)
     static constexpr int BN = BN_, STAGES = STAGES_, NEPI = NEPI_, NACC = NACC_;
+    static constexpr int kTileM = kBM * CG;        // output rows per tile (per pair)
+    static constexpr int kBRows = BN / CG;         // B rows (N) this CTA stages
     static constexpr int kStageA = kBM * kBK;
-    static constexpr int kStageB = BN * kBK;
+    static constexpr int kStageB = kBRows * kBK;
+    static constexpr int kTxBytes = CG * (kStageA + kStageB);  // landing on the leader's barrier
     static constexpr int kThreads = 32 * (2 + NEPI);
     static constexpr int kTmemCols = NACC * BN;
     static constexpr int kColGroups = NEPI / 4;    // epilogue warps per lane quadrant
@@ -48,8 +52,9 @@ struct GemmCfg {
     static constexpr int kChunks = kCols / 32;     // 32-column TMEM loads per thread
     static constexpr int kBarBytes = 8 * (2 * STAGES + 2 * NACC + 1) + 16;
     static constexpr int kSmemBytes = 1024 + STAGES * (kStageA + kStageB) + kBarBytes;
+    static_assert(CG == 1 || CG == 2, "CTA group");
     static_assert(NEPI % 4 == 0 && kCols % 32 == 0, "epilogue split");
-    static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "UMMA N for M = 128");
+    static_assert(BN % (16 * CG) == 0 && BN >= 32 && BN <= 256, "UMMA N");
     static_assert(kTmemCols == 32 || kTmemCols == 64 || kTmemCols == 128 || kTmemCols == 256 ||
                       kTmemCols == 512,
                   "TMEM allocation must be a power of two in [32, 512]");
@@ -72,11 +77,15 @@ __device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, ui
     return a | (b << 8) | (c << 16) | (d << 24);
 }
 
+// One kernel for both CTA-group sizes.  With CG = 2 the grid is made of
+// 2-CTA clusters; a pair owns a 256 x BN output tile: each CTA stages its 128
+// rows of A and its BN/2 rows of B, the leader (cluster rank 0) issues the
+// M = 256 MMAs, and each CTA's epilogue drains its own 128 TMEM lanes.
 template <class Cfg, int MODE>
 __global__ void __launch_bounds__(Cfg::kThreads, 1)
     ozaki_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ GemmParams P) {
-    constexpr int BN = Cfg::BN, STAGES = Cfg::STAGES, NACC = Cfg::NACC;
+    constexpr int CG = Cfg::CG, BN = Cfg::BN, STAGES = Cfg::STAGES, NACC = Cfg::NACC;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -92,6 +101,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;  // 0 = leader
+    const int unit = blockIdx.x / CG;                         // pair (or CTA) index
+    const int num_units = gridDim.x / CG;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -100,7 +112,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         }
         for (int a = 0; a < NACC; ++a) {
             mbar_init(tfull + a, 1);
-            mbar_init(tempty + a, Cfg::NEPI);
+            mbar_init(tempty + a, CG * Cfg::NEPI);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -111,11 +123,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         tma_prefetch_desc(&tmB);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, Cfg::kTmemCols);
-        tmem_relinquish();
+        tmem_alloc<CG>(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish<CG>();
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (CG == 2) cluster_sync();  // peers see initialised barriers before any TMA/arrive
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -125,9 +138,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             int stage = 0, issued = 0;
             uint32_t ph = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < P.num_tiles; tile += gridDim.x) {
+            for (int tile = unit; ok && tile < P.num_tiles; tile += num_units) {
                 int tm, tn;
                 tile_coords(tile, P.tiles_m, P.tiles_n, tm, tn);
+                const int arow = tm * Cfg::kTileM + (int)rank * kBM;
+                const int brow = tn * BN + (int)rank * Cfg::kBRows;
                 for (int l = 0; ok && l < P.n_mod; ++l) {
                     for (int kb = 0; kb < P.num_kb; ++kb) {
                         if (*abort_flag) { ok = false; break; }
@@ -137,32 +152,44 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                             ok = false;
                             break;
                         }
-                        mbar_arrive_expect_tx(full + stage, Cfg::kStageA + Cfg::kStageB);
-                        tma_load_3d(sA + stage * Cfg::kStageA, &tmA, full + stage, kb * kBK, tm * kBM, l);
-                        tma_load_3d(sB + stage * Cfg::kStageB, &tmB, full + stage, kb * kBK, tn * BN, l);
+                        if constexpr (CG == 1) {
+                            mbar_arrive_expect_tx(full + stage, Cfg::kTxBytes);
+                            tma_load_3d(sA + stage * Cfg::kStageA, &tmA, full + stage, kb * kBK, arow, l);
+                            tma_load_3d(sB + stage * Cfg::kStageB, &tmB, full + stage, kb * kBK, brow, l);
+                        } else {
+                            // Both CTAs' bytes land on the leader's full barrier.
+                            if (rank == 0) mbar_arrive_expect_tx(full + stage, Cfg::kTxBytes);
+                            const uint32_t fb = mapa_shared(smem_u32(full + stage), 0);
+                            tma_load_3d_pair(sA + stage * Cfg::kStageA, &tmA, fb, kb * kBK, arow, l);
+                            tma_load_3d_pair(sB + stage * Cfg::kStageB, &tmB, fb, kb * kBK, brow, l);
+                        }
                         ++issued;
                         if (++stage == STAGES) { stage = 0; ph ^= 1u; }
                     }
                 }
             }
-            // Loads still in flight must land before this CTA's shared memory goes away.
-            const int outstanding = issued < STAGES ? issued : STAGES;
-            for (int i = 0; i < outstanding; ++i) {
-                if (--stage < 0) { stage = STAGES - 1; ph ^= 1u; }
-                if (!mbar_wait(full + stage, ph, P.budget_ns)) {
-                    report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitDrainTma, stage);
-                    *abort_flag = 1;
+            // Loads still in flight must land before shared memory goes away.  The
+            // leader's full barriers count both CTAs' bytes; the peer is held by the
+            // closing cluster barrier until the leader has drained.
+            if (CG == 1 || rank == 0) {
+                const int outstanding = issued < STAGES ? issued : STAGES;
+                for (int i = 0; i < outstanding; ++i) {
+                    if (--stage < 0) { stage = STAGES - 1; ph ^= 1u; }
+                    if (!mbar_wait(full + stage, ph, P.budget_ns)) {
+                        report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitDrainTma, stage);
+                        *abort_flag = 1;
+                    }
                 }
             }
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t kIdesc = idesc_i8(kBM, BN);
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t kIdesc = idesc_i8(Cfg::kTileM, BN);
             int stage = 0, acc = 0;
             uint32_t ph = 0, aph = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < P.num_tiles; tile += gridDim.x) {
+            for (int tile = unit; ok && tile < P.num_tiles; tile += num_units) {
                 for (int l = 0; ok && l < P.n_mod; ++l) {
                     if (*abort_flag) { ok = false; break; }
                     if (!mbar_wait(tempty + acc, aph ^ 1u, P.budget_ns)) {
@@ -185,20 +212,19 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         const uint32_t b0 = smem_u32(sB + stage * Cfg::kStageB);
 #pragma unroll
                         for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
-                            mma_i8(d_tmem, smem_desc_k_sw128(a0 + kk * kUmmaK),
-                                   smem_desc_k_sw128(b0 + kk * kUmmaK), kIdesc,
-                                   (kb | kk) != 0 ? 1u : 0u);
+                            mma_i8<CG>(d_tmem, smem_desc_k_sw128(a0 + kk * kUmmaK),
+                                       smem_desc_k_sw128(b0 + kk * kUmmaK), kIdesc, (kb | kk) != 0 ? 1u : 0u);
                         }
-                        mma_commit(empty + stage);  // frees the stage once these MMAs finish
+                        mma_commit<CG>(empty + stage);  // frees the stage (in both CTAs) once done
                         if (++stage == STAGES) { stage = 0; ph ^= 1u; }
                     }
                     if (!ok) break;
-                    mma_commit(tfull + acc);  // accumulator complete
+                    mma_commit<CG>(tfull + acc);  // accumulator complete (in both CTAs)
                     if (++acc == NACC) { acc = 0; aph ^= 1u; }
                 }
             }
             // Every MMA issued above must finish before TMEM is released.
-            mma_commit(drain);
+            mma_commit_local<CG>(drain);
             if (!mbar_wait(drain, 0, P.budget_ns)) {
                 report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitDrainMma, 0);
                 *abort_flag = 1;
@@ -209,7 +235,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         const int ew = warp - 2;
         const int quad = warp & 3;  // TMEM lanes this warp may read: [32*quad, 32*quad + 32)
         const int cg = ew >> 2;     // which kCols-wide slice of the tile
-        const int row_in_tile = quad * 32 + lane;
+        const int row_in_tile = (int)rank * kBM + quad * 32 + lane;
         uint8_t* scr = nullptr;
         if (MODE == kModeCrt)
             scr = P.scratch + (int64_t)blockIdx.x * P.scratch_per_cta +
@@ -217,10 +243,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         int acc = 0;
         uint32_t aph = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; ok && tile < P.num_tiles; tile += gridDim.x) {
+        for (int tile = unit; ok && tile < P.num_tiles; tile += num_units) {
             int tm, tn;
             tile_coords(tile, P.tiles_m, P.tiles_n, tm, tn);
-            const int64_t row = (int64_t)tm * kBM + row_in_tile;
+            const int64_t row = (int64_t)tm * Cfg::kTileM + row_in_tile;
             const int col0 = tn * BN + cg * Cfg::kCols;
             for (int l = 0; l < P.n_mod; ++l) {
                 if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
@@ -271,7 +297,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(tempty + acc);
+                if (lane == 0) {
+                    if constexpr (CG == 1) mbar_arrive(tempty + acc);
+                    else mbar_arrive_cluster(mapa_shared(smem_u32(tempty + acc), 0));
+                }
                 if (++acc == NACC) { acc = 0; aph ^= 1u; }
             }
             if (!ok) break;
@@ -308,10 +337,15 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         }
     }
 
-    __syncthreads();
+    // Teardown: every role is done in this CTA; with a pair, also wait for the
+    // other CTA (the leader's MMAs read the peer's shared memory and write its
+    // TMEM), then free TMEM.
+    tc_fence_before();
+    if constexpr (CG == 2) cluster_sync();
+    else __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+        tmem_dealloc<CG>(tmem_base, Cfg::kTmemCols);
     }
 }
 

@@ -31,58 +31,110 @@ __device__ __forceinline__ double pow2(int t) {
     return __longlong_as_double((long long)(t + 1023) << 52);
 }
 
-// Scaled integer round_half_even(x * 2^s) for s in [-1024+bits, 1049] (exact: two
-// power-of-two products, then the int64 conversion rounds to nearest even).  A
-// product that underflows is below 2^-400 and rounds to 0 either way.
-__device__ __forceinline__ long long scale_round(double x, double f1, double f2) {
-    return __double2ll_rn(__dmul_rn(__dmul_rn(x, f1), f2));
+// Scaled integer round_half_even(x * 2^s) as an integer-valued double, for s in
+// [-1024+bits, 1049]: two exact power-of-two products, then rint (half to even).
+// A product that underflows is below 2^-400 and rounds to 0 either way.
+__device__ __forceinline__ double scale_round(double x, double f1, double f2) {
+    return rint(__dmul_rn(__dmul_rn(x, f1), f2));
 }
 
-// The 53-bit magnitude u of v split as u = a*2^36 + b*2^18 + c.  Then
-// u mod p == (a*(2^36 mod p) + b*(2^18 mod p) + c) mod p, and that folded sum
-// is below p*2^19; a negative v is folded to p*2^24 - t (same class as -u).
-struct Folded {
-    uint32_t a, b, c;
-    bool neg;
+// Residues of an integer-valued double x (|x| <= 2^53), floor-mod semantics.
+//
+// Step 1, per prime group (products P < 2^27, contiguous ranges of the
+// modulus list): q = floor(x * RN(1/P)) is floor(x/P) up to +-1, so
+// r0 = fma(-q, P, x) is exact and lies in [-P, 2P); r0 + (2P + 2^52) is an
+// integer in [2^52, 2^53) whose low 32 bits are y = r0 + 2P, with
+// y == x (mod P) and P <= y < 4P < 2^29.  Four FP64 operations, no conversion.
+// Step 2, per prime p of the group: y mod p by magic-number division
+// (exact for y < 2^31), three integer operations.
+struct ModTable {
+    uint32_t p[kMaxModuli], magic[kMaxModuli], shift[kMaxModuli];
 };
 
-__device__ __forceinline__ Folded fold(long long v) {
-    const unsigned long long u = v < 0 ? (unsigned long long)(-v) : (unsigned long long)v;
-    Folded f;
-    f.a = (uint32_t)(u >> 36);
-    f.b = (uint32_t)(u >> 18) & 0x3FFFFu;
-    f.c = (uint32_t)u & 0x3FFFFu;
-    f.neg = v < 0;
-    return f;
-}
-
-__device__ __forceinline__ uint32_t residue_of(const Folded& f, const ModConsts& mc, int l) {
-    uint32_t t = f.a * mc.c36[l] + f.b * mc.c18[l] + f.c;
-    t = f.neg ? mc.kneg[l] - t : t;
-    return mod_small(t, mc.p[l], mc.magic[l], mc.shift[l]);
-}
-
-// Residues of 16 consecutive elements for every modulus, stored as one 16-byte
-// vector per plane.  `dst` is plane 0 of the chunk; planes are res_plane apart.
-__device__ __forceinline__ void store_chunk_residues(const long long (&v)[16], int n_mod,
-                                                     const ModConsts& mc, int8_t* dst,
-                                                     int64_t res_plane) {
-    Folded f[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) f[j] = fold(v[j]);
-#pragma unroll 1
-    for (int l = 0; l < n_mod; ++l) {
-        uint32_t w[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const uint32_t r0 = residue_of(f[4 * q + 0], mc, l);
-            const uint32_t r1 = residue_of(f[4 * q + 1], mc, l);
-            const uint32_t r2 = residue_of(f[4 * q + 2], mc, l);
-            const uint32_t r3 = residue_of(f[4 * q + 3], mc, l);
-            w[q] = r0 | (r1 << 8) | (r2 << 16) | (r3 << 24);
-        }
-        *reinterpret_cast<uint4*>(dst + (int64_t)l * res_plane) = make_uint4(w[0], w[1], w[2], w[3]);
+constexpr ModTable make_mod_table() {
+    ModTable t{};
+    for (int i = 0; i < kMaxModuli; ++i) {
+        const uint32_t p = (uint32_t)kPrimes[i];
+        uint32_t s = 0;
+        while ((2u << s) <= p) ++s;
+        t.p[i] = p;
+        t.shift[i] = s;
+        t.magic[i] = (uint32_t)(((1ull << (32 + s)) + p - 1) / p);
     }
+    return t;
+}
+
+constexpr ModTable kModTable = make_mod_table();
+
+constexpr int kNumGroups = 5;
+constexpr int kGroupFirst[kNumGroups + 1] = {0, 8, 13, 17, 21, 25};
+
+constexpr double group_product(int g) {
+    double P = 1.0;
+    for (int i = kGroupFirst[g]; i < kGroupFirst[g + 1]; ++i) P *= (double)kPrimes[i];
+    return P;
+}
+
+template <int G>
+__device__ __forceinline__ uint32_t group_rem(double x) {
+    constexpr double P = group_product(G);
+    static_assert(P < 134217728.0, "group product must stay below 2^27");
+    constexpr double invP = 1.0 / P;
+    constexpr double off = 2.0 * P + 4503599627370496.0;  // 2P + 2^52
+    const double q = floor(__dmul_rn(x, invP));
+    const double r0 = __fma_rn(-q, P, x);
+    return (uint32_t)__double2loint(__dadd_rn(r0, off));
+}
+
+template <int L>
+__device__ __forceinline__ uint32_t prime_rem(uint32_t y) {
+    constexpr uint32_t p = kModTable.p[L], magic = kModTable.magic[L], shift = kModTable.shift[L];
+    return y - (__umulhi(y, magic) >> shift) * p;
+}
+
+template <int L>
+__device__ __forceinline__ void store_plane(const uint32_t (&y)[16], int8_t* dst, int64_t res_plane) {
+    uint32_t w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        w[q] = prime_rem<L>(y[4 * q]) | (prime_rem<L>(y[4 * q + 1]) << 8) | (prime_rem<L>(y[4 * q + 2]) << 16) |
+               (prime_rem<L>(y[4 * q + 3]) << 24);
+    *reinterpret_cast<uint4*>(dst + (int64_t)L * res_plane) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <int G, int L>
+__device__ __forceinline__ void store_group_planes(const uint32_t (&y)[16], int n_mod, int8_t* dst,
+                                                   int64_t res_plane) {
+    constexpr int end = kGroupFirst[G + 1];
+    if constexpr (L < end) {
+        if (L < n_mod) {
+            store_plane<L>(y, dst, res_plane);
+            store_group_planes<G, L + 1>(y, n_mod, dst, res_plane);
+        }
+    }
+}
+
+template <int G>
+__device__ __forceinline__ void store_groups_from(const double (&x)[16], int n_mod, int8_t* dst,
+                                                  int64_t res_plane) {
+    if constexpr (G < kNumGroups) {
+        constexpr int first = kGroupFirst[G];
+        if (first < n_mod) {
+            uint32_t y[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) y[j] = group_rem<G>(x[j]);
+            store_group_planes<G, first>(y, n_mod, dst, res_plane);
+            store_groups_from<G + 1>(x, n_mod, dst, res_plane);
+        }
+    }
+}
+
+// Residues of 16 consecutive scaled elements for every modulus, stored as one
+// 16-byte vector per plane.  `dst` is plane 0 of the chunk; planes are
+// res_plane apart.
+__device__ __forceinline__ void store_chunk_residues(const double (&x)[16], int n_mod, int8_t* dst,
+                                                     int64_t res_plane) {
+    store_groups_from<0>(x, n_mod, dst, res_plane);
 }
 
 // ---------------------------------------------------------------------------
@@ -154,7 +206,7 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const __grid_constant__
         int8_t* out_row = P.res + row * P.res_ld;
         for (int64_t c = gt; c < nchunk_out; c += GROUP) {
             const int64_t t0 = c * 16;
-            long long v[16];
+            double v[16];
             if (finite && VEC && t0 + 16 <= P.k) {
                 const double2* p2 = reinterpret_cast<const double2*>(x + t0);
 #pragma unroll
@@ -166,9 +218,9 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const __grid_constant__
             } else {
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
-                    v[j] = (finite && t0 + j < P.k) ? scale_round(__ldg(x + t0 + j), f1, f2) : 0;
+                    v[j] = (finite && t0 + j < P.k) ? scale_round(__ldg(x + t0 + j), f1, f2) : 0.0;
             }
-            store_chunk_residues(v, P.n_mod, P.mc, out_row + t0, P.res_plane);
+            store_chunk_residues(v, P.n_mod, out_row + t0, P.res_plane);
         }
     }
 }
@@ -232,11 +284,11 @@ __global__ void __launch_bounds__(256) split_strided_kernel(const __grid_constan
     const bool finite = e != kNonFiniteExp;
     const int s = P.bits - e;
     const double f1 = pow2(s >> 1), f2 = pow2(s - (s >> 1));
-    long long v[16];
+    double v[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j)
-        v[j] = (finite && t0 + j < P.k) ? scale_round(tile[16 * kc + j][lr ^ ((kc & 7) << 2)], f1, f2) : 0;
-    store_chunk_residues(v, P.n_mod, P.mc, P.res + row * P.res_ld + t0, P.res_plane);
+        v[j] = (finite && t0 + j < P.k) ? scale_round(tile[16 * kc + j][lr ^ ((kc & 7) << 2)], f1, f2) : 0.0;
+    store_chunk_residues(v, P.n_mod, P.res + row * P.res_ld + t0, P.res_plane);
 }
 
 }  // namespace fpemu

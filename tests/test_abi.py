@@ -126,3 +126,40 @@ def test_python_layer_errors_without_gpu():
         ozaki2_int8_matmul(torch.ones(2, 2, dtype=torch.int32), torch.ones(2, 2, dtype=torch.int32))
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         ozaki2_int8_matmul(torch.ones(2, 2, dtype=torch.float64), torch.ones(2, 2, dtype=torch.float64))
+
+
+# The split kernel's residue path (split_kernels.cuh): the scaled value x (an
+# integer-valued double, |x| <= 2^53) is reduced modulo 5 prime groups in FP64
+# -- q = floor(x * RN(1/P)), r0 = fma(-q, P, x) (exact), y = low word of
+# r0 + (2P + 2^52) -- and each prime then takes y mod p by magic division.
+PRIME_GROUPS = [(0, 8), (8, 13), (13, 17), (17, 21), (21, 25)]
+
+
+def test_prime_groups_cover_moduli_and_fit():
+    assert PRIME_GROUPS[0][0] == 0 and PRIME_GROUPS[-1][1] == 25
+    for (a, b), (c, _) in zip(PRIME_GROUPS, PRIME_GROUPS[1:]):
+        assert b == c
+    for a, b in PRIME_GROUPS:
+        P = int(np.prod(oo.PRIMES[a:b], dtype=object))
+        assert P < 2 ** 27  # so r0 + 2P stays in [P, 4P) < 2^29 < 2^31
+
+
+def test_group_reduction_exact():
+    rng = np.random.default_rng(2)
+    x = np.concatenate([rng.integers(-(2 ** 53), 2 ** 53 + 1, 200_000, dtype=np.int64),
+                        np.array([0, 1, -1, 2 ** 53, -(2 ** 53), 2 ** 52 + 1, -(2 ** 52) - 1], dtype=np.int64)])
+    xd = x.astype(np.float64)
+    assert np.all(xd.astype(np.int64) == x)
+    for a, b in PRIME_GROUPS:
+        P = int(np.prod(oo.PRIMES[a:b], dtype=object))
+        invP = np.float64(1.0) / np.float64(P)
+        q = np.floor(xd * invP)                       # FP64 multiply (RN), floor
+        r0 = x - q.astype(np.int64) * P               # the fma is exact: integer arithmetic
+        assert np.all(r0 >= -P) and np.all(r0 < 2 * P)
+        y = r0 + 2 * P                                # low word of r0 + (2P + 2^52)
+        assert np.all(y >= P) and np.all(y < 2 ** 31)
+        for p in oo.PRIMES[a:b]:
+            s, magic = _mod_consts(p)
+            yu = y.astype(np.uint64)
+            r = yu - ((yu * np.uint64(magic)) >> np.uint64(32 + s)) * np.uint64(p)
+            np.testing.assert_array_equal(r.astype(np.int64), np.mod(x, p))

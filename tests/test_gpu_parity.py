@@ -228,12 +228,12 @@ def test_convert_mlp_matches_reference(torch_cuda):
     assert model[0].weight.dtype == torch.float64
     # Each emulated Linear on its own input is bit-exact vs the oracle.
     h = x.reshape(-1, 4)
-    for layer in (model[0], model[2]):
-        got = layer(h).detach().cpu().numpy()
-        want = oo.ozaki2_matmul(h.cpu().numpy(), layer.weight.detach().cpu().numpy().T) + \
-            layer.bias.detach().cpu().numpy()
-        np.testing.assert_array_equal(got.view(np.int64), want.view(np.int64))
-        h = torch.tanh(layer(h))
+    with torch.no_grad():
+        for layer in (model[0], model[2]):
+            got = layer(h).cpu().numpy()
+            want = oo.ozaki2_matmul(h.cpu().numpy(), layer.weight.cpu().numpy().T) + layer.bias.cpu().numpy()
+            np.testing.assert_array_equal(got.view(np.int64), want.view(np.int64))
+            h = torch.tanh(layer(h))
 
 
 def test_backward_matches_reference(torch_cuda):
@@ -267,3 +267,26 @@ def test_nonfinite_rows_give_nan(torch_cuda):
     B[4, 1] = 0.0
     want = oo.ozaki2_matmul(A, B)
     np.testing.assert_array_equal(C[mask], want[mask])
+
+
+@pytest.mark.parametrize("ctas", ["1", "2"])
+@pytest.mark.parametrize("m,k,n", [(300, 520, 700), (513, 1100, 257), (1000, 300, 1000)])
+def test_gemm_configurations_agree(torch_cuda, monkeypatch, ctas, m, k, n):
+    """The CTA-pair GEMM (default) and the single-CTA GEMM (FPEMU_GEMM_CTAS=1)
+    are independent kernels; both must reproduce the oracle bit for bit, in the
+    fused mode and in both parity taps."""
+    torch = torch_cuda
+    from fp_emulation import ozaki2_int8_matmul
+    from fp_emulation.ozaki import _matmul_residues, _split
+
+    monkeypatch.setenv("FPEMU_GEMM_CTAS", ctas)
+    A, B = _rand_case(m + k + n, m, k, n, kind="wide")
+    C, st = oo.ozaki2_matmul(A, B, stages=True)
+    got = ozaki2_int8_matmul(_cuda(torch, A), _cuda(torch, B)).cpu().numpy()
+    np.testing.assert_array_equal(got.view(np.int64), C.view(np.int64))
+    a_res, _ = _split(_cuda(torch, A), 53, len(st["moduli"]))
+    b_res, _ = _split(_cuda(torch, B).T, 53, len(st["moduli"]))
+    raw = _matmul_residues(a_res, b_res, st["moduli"], raw=True).cpu().numpy()
+    np.testing.assert_array_equal(raw, oo.matmul_residues_raw(st["a_res"], st["b_res"]).astype(np.int32))
+    res = _matmul_residues(a_res, b_res, st["moduli"]).cpu().numpy()
+    np.testing.assert_array_equal(res.astype(np.int32), st["res"])
