@@ -343,7 +343,7 @@ int launch_split(const SplitParams& P, uint64_t* colmax, const DevInfo& d, cudaS
 
 template <class Cfg, int MODE>
 int launch_gemm_cfg(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int64_t res_ld, const DevInfo& d,
-                    cudaStream_t st) {
+                    cudaStream_t st, int max_ctas) {
     const int64_t m = P.m, n = P.n;
     const int64_t res_plane_a = m * res_ld, res_plane_b = n * res_ld;
     CUtensorMap ta, tb;
@@ -355,7 +355,8 @@ int launch_gemm_cfg(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int
     P.num_tiles = P.tiles_m * P.tiles_n;
     P.budget_ns = wait_budget_ns();
     mod_consts(P.n_mod, &P.mc);
-    const int units = gemm_units<Cfg>(d, m, n);
+    int units = gemm_units<Cfg>(d, m, n);
+    if (max_ctas > 0 && units > max_ctas / Cfg::CG) units = max_ctas / Cfg::CG;
     if (units < 1) return fail(FPEMU_ERR_CUDA, "GEMM kernel cannot be made resident on this device");
     auto kern = ozaki_gemm_kernel<Cfg, MODE>;
     FPEMU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
@@ -377,10 +378,39 @@ int launch_gemm_cfg(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int
 
 template <int MODE>
 int launch_gemm(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int64_t res_ld, const DevInfo& d,
-                cudaStream_t st) {
+                cudaStream_t st, int max_ctas = 0) {
     if (P.m == 0 || P.n == 0) return FPEMU_OK;
-    return use_pairs() ? launch_gemm_cfg<MainCfg, MODE>(P, a_res, b_res, res_ld, d, st)
-                       : launch_gemm_cfg<SingleCfg, MODE>(P, a_res, b_res, res_ld, d, st);
+    return use_pairs() ? launch_gemm_cfg<MainCfg, MODE>(P, a_res, b_res, res_ld, d, st, max_ctas)
+                       : launch_gemm_cfg<SingleCfg, MODE>(P, a_res, b_res, res_ld, d, st, max_ctas);
+}
+
+// ---------------------------------------------- allocation-free staging --
+//
+// Staging area of fpemu_gemm_crt_noalloc, for callers that must not allocate
+// device memory.  It is part of this library's device image: every GPU on
+// which the library's kernels are loaded holds these 64 MiB until the process
+// exits.  Host code only ever sees the symbol as a stand-in; the device
+// address comes from cudaGetSymbolAddress, once per device.
+constexpr size_t kNoAllocScratchBytes = (size_t)FPEMU_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+int noalloc_scratch(uint8_t** out) {
+    static std::mutex mu;
+    static uint8_t* addr[64] = {};
+    int dev = 0;
+    FPEMU_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(FPEMU_ERR_NO_DEVICE, "device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lk(mu);
+    if (addr[dev] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return fail(FPEMU_ERR_CUDA, "cudaGetSymbolAddress(staging area) failed on device %d: %s", dev,
+                        cudaGetErrorString(e));
+        addr[dev] = static_cast<uint8_t*>(p);
+    }
+    *out = addr[dev];
+    return FPEMU_OK;
 }
 
 int check_gemm_args(int64_t m, int64_t n, int64_t k, int n_mod, const void* a_res, const void* b_res,
@@ -563,6 +593,44 @@ int fpemu_gemm_crt(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_r
     P.scratch_per_cta = MainCfg::scratch_per_cta(n_mod);
     FPEMU_TRY(crt_weights(n_mod, &P.cc));
     return launch_gemm<kModeCrt>(P, a_res, b_res, res_ld, d, static_cast<cudaStream_t>(stream));
+}
+
+int fpemu_gemm_crt_noalloc(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_res,
+                           const int8_t* b_res, int64_t res_ld, const int32_t* row_exp,
+                           const int32_t* col_exp, int bits, double* C, int64_t ldc, void* stream) {
+    DevInfo d;
+    FPEMU_TRY(device_info(&d));
+    FPEMU_TRY(bits_ok(bits));
+    FPEMU_TRY(check_gemm_args(m, n, k, n_mod, a_res, b_res, res_ld));
+    if (m == 0 || n == 0) return FPEMU_OK;
+    if (!row_exp || !col_exp || !C || ldc < n)
+        return fail(FPEMU_ERR_INVALID, "gemm_crt_noalloc: bad output arguments");
+    // Each CTA stages n_mod * 128 * 256 bytes; the grid shrinks to what the
+    // static area holds, and a modulus count that cannot fit one CTA pair is refused.
+    const int64_t per_cta = MainCfg::scratch_per_cta(n_mod);
+    const int64_t fit = (int64_t)kNoAllocScratchBytes / per_cta;
+    if (fit < 2)
+        return fail(FPEMU_ERR_WORKSPACE,
+                    "gemm_crt_noalloc: n_mod=%d needs %lld bytes per CTA pair, more than the %zu-byte static "
+                    "staging area", n_mod, (long long)(2 * per_cta), kNoAllocScratchBytes);
+    uint8_t* scratch = nullptr;
+    FPEMU_TRY(noalloc_scratch(&scratch));
+    GemmParams P;
+    memset(&P, 0, sizeof P);
+    P.m = (int)m;
+    P.n = (int)n;
+    P.k = (int)k;
+    P.n_mod = n_mod;
+    P.C = C;
+    P.ldc = ldc;
+    P.row_exp = row_exp;
+    P.col_exp = col_exp;
+    P.two_bits = 2 * bits;
+    P.scratch = scratch;
+    P.scratch_per_cta = per_cta;
+    FPEMU_TRY(crt_weights(n_mod, &P.cc));
+    const int max_ctas = (int)std::min<int64_t>(fit & ~(int64_t)1, 1 << 20);
+    return launch_gemm<kModeCrt>(P, a_res, b_res, res_ld, d, static_cast<cudaStream_t>(stream), max_ctas);
 }
 
 int fpemu_ozaki2_dgemm(int64_t m, int64_t n, int64_t k, const double* A, int64_t sA_row, int64_t sA_col,

@@ -42,6 +42,7 @@ SIGNATURES = {
     "fpemu_gemm_crt": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _vp, _vp, _int, _vp, _i64,
                               _vp, _sz, _vp]),
     "fpemu_gemm_workspace_size": (_sz, [_i64, _i64, _int]),
+    "fpemu_gemm_crt_noalloc": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _vp, _vp, _int, _vp, _i64, _vp]),
     "fpemu_device_error": (_int, [_IP, _IP, _IP, _IP, _int]),
 }
 

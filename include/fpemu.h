@@ -120,6 +120,31 @@ int fpemu_gemm_crt(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t *a_r
                    const int32_t *col_exp, int bits, double *C, int64_t ldc, void *workspace,
                    size_t workspace_bytes, void *stream);
 
+/* Allocation-free variant of fpemu_gemm_crt.  It has no counterpart in the
+ * reference.  For callers that cannot allocate device memory -- code running
+ * where cudaMalloc is not allowed (inside a host application that owns the
+ * allocator, or a runtime that forbids allocation between launches) -- it
+ * needs no workspace argument: the fused kernel stages its residues in a
+ * static device array of FPEMU_NOALLOC_SCRATCH_BYTES (64 MiB) that is part of
+ * the library, so every GPU that loads the library holds it until the process
+ * exits.  The caller still passes all inputs and the output C.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) and caches it; make that first call before any
+ *    stream capture.
+ *  - The kernel grid shrinks to the CTAs whose staging fits the array
+ *    (n_mod * 32 KiB per CTA: 80 CTAs at n_mod = 25), so large problems run
+ *    slower than through fpemu_gemm_crt; a modulus count whose staging does not
+ *    fit one CTA pair is rejected with FPEMU_ERR_WORKSPACE.
+ *  - All calls share the array and it keeps the last call's contents (nothing
+ *    in it needs to start at zero).  Calls that overlap on the GPU -- on two
+ *    streams, or from two host threads -- race on it and corrupt each other.
+ *  - Calls no cudaMalloc, cudaFree or other allocating routine. */
+#define FPEMU_NOALLOC_SCRATCH_BYTES (64u << 20)
+int fpemu_gemm_crt_noalloc(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t *a_res,
+                           const int8_t *b_res, int64_t res_ld, const int32_t *row_exp,
+                           const int32_t *col_exp, int bits, double *C, int64_t ldc,
+                           void *stream);
+
 /* Workspace bytes fpemu_gemm_crt / fpemu_gemm_residues need (the epilogue's
  * per-CTA residue staging). */
 size_t fpemu_gemm_workspace_size(int64_t m, int64_t n, int n_mod);
