@@ -278,10 +278,30 @@ int gemm_ctas(const DevInfo& d, int64_t m, int64_t n) {
     return use_pairs() ? 2 * gemm_units<MainCfg>(d, m, n) : gemm_units<SingleCfg>(d, m, n);
 }
 
-size_t gemm_scratch_bytes(const DevInfo& d, int64_t m, int64_t n, int n_mod) {
-    // Per CTA the staging is the same for both configurations (128 x 256 outputs).
-    const int64_t ctas = std::max(2 * (int64_t)gemm_units<MainCfg>(d, m, n), (int64_t)gemm_units<SingleCfg>(d, m, n));
-    return align256((size_t)ctas * (size_t)MainCfg::scratch_per_cta(n_mod));
+// Schedule of the fused kernel: modulus-major unless FPEMU_GEMM_SCHED=tile.
+int gemm_sched() {
+    const char* s = getenv("FPEMU_GEMM_SCHED");
+    return (s && strcmp(s, "tile") == 0) ? kSchedTileMajor : kSchedModulusMajor;
+}
+
+template <class Cfg>
+int64_t staging_slots(const DevInfo& d, int64_t m, int64_t n, int sched) {
+    if (sched == kSchedTileMajor) return (int64_t)gemm_units<Cfg>(d, m, n) * Cfg::CG;  // one per CTA
+    const int64_t tiles = ((m + Cfg::kTileM - 1) / Cfg::kTileM) * ((n + Cfg::BN - 1) / Cfg::BN);
+    return tiles * Cfg::CG;  // one per CTA share of every tile
+}
+
+// Staging bytes of the fused kernel; covers both GEMM configurations (their
+// slots are the same size: one CTA's 128 x 256 share of a tile).
+size_t gemm_scratch_bytes(const DevInfo& d, int64_t m, int64_t n, int n_mod, int sched) {
+    static_assert(MainCfg::kBRows * MainCfg::CG == SingleCfg::BN, "slot sizes agree");
+    const int64_t slots = std::max(staging_slots<MainCfg>(d, m, n, sched), staging_slots<SingleCfg>(d, m, n, sched));
+    // Plus the per-pass counters of the modulus-major schedule, after the slots.
+    return align256((size_t)slots * (size_t)MainCfg::slot_bytes(n_mod)) + 256;
+}
+
+size_t pass_ctr_offset(const DevInfo& d, int64_t m, int64_t n, int n_mod, int sched) {
+    return gemm_scratch_bytes(d, m, n, n_mod, sched) - 256;
 }
 
 struct Layout {
@@ -298,7 +318,7 @@ Layout layout(const DevInfo& d, int64_t m, int64_t n, int64_t k, int n_mod) {
     L.row_exp = off; off += align256((size_t)m * 4);
     L.col_exp = off; off += align256((size_t)n * 4);
     L.colmax = off; off += align256((size_t)(m > n ? m : n) * 8);
-    L.scratch = off; off += gemm_scratch_bytes(d, m, n, n_mod);
+    L.scratch = off; off += gemm_scratch_bytes(d, m, n, n_mod, gemm_sched());
     L.total = off;
     return L;
 }
@@ -486,7 +506,7 @@ int64_t fpemu_max_k(int n_mod) { return max_k(n_mod); }
 size_t fpemu_gemm_workspace_size(int64_t m, int64_t n, int n_mod) {
     DevInfo d;
     if (device_info(&d) != FPEMU_OK || m < 0 || n < 0 || n_mod < 1 || n_mod > kMaxModuli) return 0;
-    return gemm_scratch_bytes(d, m, n, n_mod);
+    return gemm_scratch_bytes(d, m, n, n_mod, gemm_sched());
 }
 
 size_t fpemu_workspace_size(int64_t m, int64_t n, int64_t k, int n_mod) {
@@ -574,7 +594,8 @@ int fpemu_gemm_crt(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_r
     FPEMU_TRY(check_gemm_args(m, n, k, n_mod, a_res, b_res, res_ld));
     if (m == 0 || n == 0) return FPEMU_OK;
     if (!row_exp || !col_exp || !C || ldc < n) return fail(FPEMU_ERR_INVALID, "gemm_crt: bad output arguments");
-    const size_t need = gemm_scratch_bytes(d, m, n, n_mod);
+    const int sched = gemm_sched();
+    const size_t need = gemm_scratch_bytes(d, m, n, n_mod, sched);
     if (workspace == nullptr || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
         return fail(FPEMU_ERR_WORKSPACE, "gemm_crt: need %zu bytes of 256-byte aligned workspace, got %zu",
                     need, workspace_bytes);
@@ -590,7 +611,12 @@ int fpemu_gemm_crt(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_r
     P.col_exp = col_exp;
     P.two_bits = 2 * bits;
     P.scratch = static_cast<uint8_t*>(workspace);
-    P.scratch_per_cta = MainCfg::scratch_per_cta(n_mod);
+    P.scratch_slot = MainCfg::slot_bytes(n_mod);
+    P.sched = sched;
+    if (sched == kSchedModulusMajor) {
+        P.pass_ctr = reinterpret_cast<unsigned int*>(P.scratch + pass_ctr_offset(d, m, n, n_mod, sched));
+        FPEMU_CUDA(cudaMemsetAsync(P.pass_ctr, 0, 256, static_cast<cudaStream_t>(stream)));
+    }
     FPEMU_TRY(crt_weights(n_mod, &P.cc));
     return launch_gemm<kModeCrt>(P, a_res, b_res, res_ld, d, static_cast<cudaStream_t>(stream));
 }
@@ -607,7 +633,7 @@ int fpemu_gemm_crt_noalloc(int64_t m, int64_t n, int64_t k, int n_mod, const int
         return fail(FPEMU_ERR_INVALID, "gemm_crt_noalloc: bad output arguments");
     // Each CTA stages n_mod * 128 * 256 bytes; the grid shrinks to what the
     // static area holds, and a modulus count that cannot fit one CTA pair is refused.
-    const int64_t per_cta = MainCfg::scratch_per_cta(n_mod);
+    const int64_t per_cta = MainCfg::slot_bytes(n_mod);
     const int64_t fit = (int64_t)kNoAllocScratchBytes / per_cta;
     if (fit < 2)
         return fail(FPEMU_ERR_WORKSPACE,
@@ -627,7 +653,8 @@ int fpemu_gemm_crt_noalloc(int64_t m, int64_t n, int64_t k, int n_mod, const int
     P.col_exp = col_exp;
     P.two_bits = 2 * bits;
     P.scratch = scratch;
-    P.scratch_per_cta = per_cta;
+    P.scratch_slot = per_cta;
+    P.sched = kSchedTileMajor;  // one reusable slot per CTA: bounded staging
     FPEMU_TRY(crt_weights(n_mod, &P.cc));
     const int max_ctas = (int)std::min<int64_t>(fit & ~(int64_t)1, 1 << 20);
     return launch_gemm<kModeCrt>(P, a_res, b_res, res_ld, d, static_cast<cudaStream_t>(stream), max_ctas);

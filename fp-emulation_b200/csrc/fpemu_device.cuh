@@ -30,6 +30,7 @@ enum : int {
     kWaitTmemEmpty = 4,  // MMA warp waiting for the epilogue to drain TMEM
     kWaitDrainTma = 5,   // producer draining its loads at exit
     kWaitDrainMma = 6,   // MMA warp draining its MMAs at exit
+    kWaitPass = 7,       // producer waiting for every CTA to finish issuing a modulus pass
 };
 
 // The first device-side failure on this device (one copy per device that loads

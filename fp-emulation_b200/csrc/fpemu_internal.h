@@ -47,6 +47,16 @@ struct SplitParams {
 
 enum GemmMode : int { kModeRaw = 0, kModeResidue = 1, kModeCrt = 2 };
 
+// Order in which a CTA (pair) walks its (tile, modulus) units.
+//   kSchedModulusMajor: every CTA owns a fixed set of tiles and sweeps them once per
+//     modulus, so at any time all CTAs read the same modulus plane of A and B
+//     (L2 reuse as in one plain GEMM); residues are staged per tile (workspace
+//     n_mod bytes per output element).
+//   kSchedTileMajor: all moduli of a tile back to back; staging is one reusable
+//     slot per CTA (bounded workspace), at the cost of re-reading A and B strips
+//     from DRAM for every modulus.
+enum GemmSched : int { kSchedModulusMajor = 0, kSchedTileMajor = 1 };
+
 struct GemmParams {
     int m, n, k, n_mod;
     int num_kb;            // ceil(k / 128)
@@ -57,8 +67,10 @@ struct GemmParams {
     const int32_t* row_exp;
     const int32_t* col_exp;
     int two_bits;
-    uint8_t* scratch;      // mode 2: per-CTA residue staging
-    int64_t scratch_per_cta;
+    uint8_t* scratch;      // mode 2: residue staging
+    int64_t scratch_slot;  // bytes of one staging slot (one CTA's share of one tile)
+    int sched;             // GemmSched
+    unsigned int* pass_ctr;  // modulus-major: n_mod zeroed counters aligning the producers per pass
     uint64_t budget_ns;    // bound on every mbarrier wait
     ModConsts mc;
     CrtConsts cc;

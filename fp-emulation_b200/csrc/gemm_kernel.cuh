@@ -59,8 +59,9 @@ struct GemmCfg {
                       kTmemCols == 512,
                   "TMEM allocation must be a power of two in [32, 512]");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory");
-    // Residue staging for mode 2: every epilogue thread owns n_mod * kCols bytes.
-    static int64_t scratch_per_cta(int n_mod) { return (int64_t)n_mod * kBM * BN; }
+    // One staging slot (mode 2): one CTA's 128 x BN share of a tile, n_mod bytes per
+    // output (each epilogue thread owns n_mod * kCols bytes of it).
+    static int64_t slot_bytes(int n_mod) { return (int64_t)n_mod * kBM * BN; }
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
@@ -132,40 +133,77 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
+    // This CTA (pair) owns tiles r = unit, unit + num_units, ... (in band-raster
+    // order) and walks (tile, modulus) units in the order P.sched selects.  All
+    // three roles generate the same sequence.
+    const int my_tiles = (P.num_tiles - unit + num_units - 1) / num_units;
+    const int my_units = my_tiles * P.n_mod;
+    auto unit_at = [&](int idx, int& tile, int& l) {
+        int i;
+        if (P.sched == kSchedTileMajor) {
+            i = idx / P.n_mod;
+            l = idx - i * P.n_mod;
+        } else {
+            l = idx / my_tiles;
+            i = idx - l * my_tiles;
+        }
+        tile = i * num_units + unit;
+    };
+
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             int stage = 0, issued = 0;
             uint32_t ph = 0;
             bool ok = true;
-            for (int tile = unit; ok && tile < P.num_tiles; tile += num_units) {
-                int tm, tn;
-                tile_coords(tile, P.tiles_m, P.tiles_n, tm, tn);
-                const int arow = tm * Cfg::kTileM + (int)rank * kBM;
-                const int brow = tn * BN + (int)rank * Cfg::kBRows;
-                for (int l = 0; ok && l < P.n_mod; ++l) {
-                    for (int kb = 0; kb < P.num_kb; ++kb) {
-                        if (*abort_flag) { ok = false; break; }
-                        if (!mbar_wait(empty + stage, ph ^ 1u, P.budget_ns)) {
-                            report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitEmpty, tile);
+            for (int idx = 0; ok && idx < my_units; ++idx) {
+                int tile, l, tm, tn;
+                unit_at(idx, tile, l);
+                if (P.pass_ctr != nullptr && l > 0 && idx == l * my_tiles) {
+                    // Modulus-major: start pass l only when every CTA has issued all of
+                    // pass l-1, so the whole grid streams one modulus plane at a time and
+                    // its A band stays in L2 (pairs with one tile fewer would otherwise
+                    // drift a unit further ahead every pass).  All CTAs are co-resident
+                    // (the grid is sized to the device's active-cluster limit); the wait
+                    // is bounded like every other.
+                    atomicAdd(P.pass_ctr + l, 1u);
+                    const volatile unsigned int* c = P.pass_ctr + l;
+                    const uint64_t t0 = global_ns();
+                    while (*c < gridDim.x) {
+                        if (*abort_flag || global_ns() - t0 > P.budget_ns) {
+                            report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitPass, l);
                             *abort_flag = 1;
                             ok = false;
                             break;
                         }
-                        if constexpr (CG == 1) {
-                            mbar_arrive_expect_tx(full + stage, Cfg::kTxBytes);
-                            tma_load_3d(sA + stage * Cfg::kStageA, &tmA, full + stage, kb * kBK, arow, l);
-                            tma_load_3d(sB + stage * Cfg::kStageB, &tmB, full + stage, kb * kBK, brow, l);
-                        } else {
-                            // Both CTAs' bytes land on the leader's full barrier.
-                            if (rank == 0) mbar_arrive_expect_tx(full + stage, Cfg::kTxBytes);
-                            const uint32_t fb = mapa_shared(smem_u32(full + stage), 0);
-                            tma_load_3d_pair(sA + stage * Cfg::kStageA, &tmA, fb, kb * kBK, arow, l);
-                            tma_load_3d_pair(sB + stage * Cfg::kStageB, &tmB, fb, kb * kBK, brow, l);
-                        }
-                        ++issued;
-                        if (++stage == STAGES) { stage = 0; ph ^= 1u; }
+                        __nanosleep(64);
                     }
+                    if (!ok) break;
+                }
+                tile_coords(tile, P.tiles_m, P.tiles_n, tm, tn);
+                const int arow = tm * Cfg::kTileM + (int)rank * kBM;
+                const int brow = tn * BN + (int)rank * Cfg::kBRows;
+                for (int kb = 0; kb < P.num_kb; ++kb) {
+                    if (*abort_flag) { ok = false; break; }
+                    if (!mbar_wait(empty + stage, ph ^ 1u, P.budget_ns)) {
+                        report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitEmpty, tile);
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    if constexpr (CG == 1) {
+                        mbar_arrive_expect_tx(full + stage, Cfg::kTxBytes);
+                        tma_load_3d(sA + stage * Cfg::kStageA, &tmA, full + stage, kb * kBK, arow, l);
+                        tma_load_3d(sB + stage * Cfg::kStageB, &tmB, full + stage, kb * kBK, brow, l);
+                    } else {
+                        // Both CTAs' bytes land on the leader's full barrier.
+                        if (rank == 0) mbar_arrive_expect_tx(full + stage, Cfg::kTxBytes);
+                        const uint32_t fb = mapa_shared(smem_u32(full + stage), 0);
+                        tma_load_3d_pair(sA + stage * Cfg::kStageA, &tmA, fb, kb * kBK, arow, l);
+                        tma_load_3d_pair(sB + stage * Cfg::kStageB, &tmB, fb, kb * kBK, brow, l);
+                    }
+                    ++issued;
+                    if (++stage == STAGES) { stage = 0; ph ^= 1u; }
                 }
             }
             // Loads still in flight must land before shared memory goes away.  The
@@ -189,39 +227,37 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             int stage = 0, acc = 0;
             uint32_t ph = 0, aph = 0;
             bool ok = true;
-            for (int tile = unit; ok && tile < P.num_tiles; tile += num_units) {
-                for (int l = 0; ok && l < P.n_mod; ++l) {
-                    if (*abort_flag) { ok = false; break; }
-                    if (!mbar_wait(tempty + acc, aph ^ 1u, P.budget_ns)) {
-                        report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitTmemEmpty, tile);
+            for (int idx = 0; ok && idx < my_units; ++idx) {
+                if (*abort_flag) { ok = false; break; }
+                if (!mbar_wait(tempty + acc, aph ^ 1u, P.budget_ns)) {
+                    report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitTmemEmpty, idx);
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < P.num_kb; ++kb) {
+                    if (!mbar_wait(full + stage, ph, P.budget_ns)) {
+                        report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitFull, idx);
                         *abort_flag = 1;
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-                    for (int kb = 0; kb < P.num_kb; ++kb) {
-                        if (!mbar_wait(full + stage, ph, P.budget_ns)) {
-                            report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitFull, tile);
-                            *abort_flag = 1;
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        const uint32_t a0 = smem_u32(sA + stage * Cfg::kStageA);
-                        const uint32_t b0 = smem_u32(sB + stage * Cfg::kStageB);
+                    const uint32_t a0 = smem_u32(sA + stage * Cfg::kStageA);
+                    const uint32_t b0 = smem_u32(sB + stage * Cfg::kStageB);
 #pragma unroll
-                        for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
-                            mma_i8<CG>(d_tmem, smem_desc_k_sw128(a0 + kk * kUmmaK),
-                                       smem_desc_k_sw128(b0 + kk * kUmmaK), kIdesc, (kb | kk) != 0 ? 1u : 0u);
-                        }
-                        mma_commit<CG>(empty + stage);  // frees the stage (in both CTAs) once done
-                        if (++stage == STAGES) { stage = 0; ph ^= 1u; }
+                    for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+                        mma_i8<CG>(d_tmem, smem_desc_k_sw128(a0 + kk * kUmmaK), smem_desc_k_sw128(b0 + kk * kUmmaK),
+                                   kIdesc, (kb | kk) != 0 ? 1u : 0u);
                     }
-                    if (!ok) break;
-                    mma_commit<CG>(tfull + acc);  // accumulator complete (in both CTAs)
-                    if (++acc == NACC) { acc = 0; aph ^= 1u; }
+                    mma_commit<CG>(empty + stage);  // frees the stage (in both CTAs) once done
+                    if (++stage == STAGES) { stage = 0; ph ^= 1u; }
                 }
+                if (!ok) break;
+                mma_commit<CG>(tfull + acc);  // accumulator complete (in both CTAs)
+                if (++acc == NACC) { acc = 0; aph ^= 1u; }
             }
             // Every MMA issued above must finish before TMEM is released.
             mma_commit_local<CG>(drain);
@@ -232,105 +268,118 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         }
     } else {
         // ------------------------------------------------------------ epilogue
+        constexpr int kChunks = Cfg::kChunks;
         const int ew = warp - 2;
         const int quad = warp & 3;  // TMEM lanes this warp may read: [32*quad, 32*quad + 32)
         const int cg = ew >> 2;     // which kCols-wide slice of the tile
         const int row_in_tile = (int)rank * kBM + quad * 32 + lane;
-        uint8_t* scr = nullptr;
-        if (MODE == kModeCrt)
-            scr = P.scratch + (int64_t)blockIdx.x * P.scratch_per_cta +
-                  ((int64_t)ew * P.n_mod * Cfg::kChunks * 32 + lane) * 32;
+        // This thread's part of a staging slot: for modulus l and chunk c the 32
+        // bytes at ((ew*n_mod + l)*kChunks + c)*1 KiB + lane*32 (a warp's stores
+        // cover one contiguous KiB).  Only this thread reads them back.
+        const int64_t thread_off = ((int64_t)ew * P.n_mod * kChunks * 32 + lane) * 32;
         int acc = 0;
         uint32_t aph = 0;
         bool ok = true;
-        for (int tile = unit; ok && tile < P.num_tiles; tile += num_units) {
-            int tm, tn;
+        for (int idx = 0; ok && idx < my_units; ++idx) {
+            int tile, l, tm, tn;
+            unit_at(idx, tile, l);
             tile_coords(tile, P.tiles_m, P.tiles_n, tm, tn);
             const int64_t row = (int64_t)tm * Cfg::kTileM + row_in_tile;
             const int col0 = tn * BN + cg * Cfg::kCols;
-            for (int l = 0; l < P.n_mod; ++l) {
-                if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
-                bool got = mbar_wait(tfull + acc, aph, P.budget_ns);
-                got = __all_sync(0xffffffffu, got);
-                if (!got) {
-                    if (lane == 0) report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitTmemFull, tile);
-                    *abort_flag = 1;
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t taddr =
-                    tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + cg * Cfg::kCols);
-                const uint32_t p = P.mc.p[l], mg = P.mc.magic[l], sh = P.mc.shift[l];
+            uint8_t* scr = nullptr;
+            if (MODE == kModeCrt) {
+                const int64_t slot = P.sched == kSchedTileMajor ? (int64_t)blockIdx.x : (int64_t)tile * CG + rank;
+                scr = P.scratch + slot * P.scratch_slot + thread_off;
+            }
+            const bool last = (l == P.n_mod - 1);
+
+            if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
+            bool got = mbar_wait(tfull + acc, aph, P.budget_ns);
+            got = __all_sync(0xffffffffu, got);
+            if (!got) {
+                if (lane == 0) report_error(&g_device_error, FPEMU_ERR_TIMEOUT, kWaitTmemFull, idx);
+                *abort_flag = 1;
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t taddr =
+                tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + cg * Cfg::kCols);
+            const uint32_t p = P.mc.p[l], mg = P.mc.magic[l], sh = P.mc.shift[l];
 #pragma unroll 1
-                for (int c = 0; c < Cfg::kChunks; ++c) {
-                    uint32_t v[32];
-                    tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), v);
-                    tmem_ld_wait();
-                    const int cb = col0 + c * 32;
-                    if (MODE == kModeRaw) {
+            for (int c = 0; c < kChunks; ++c) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), v);
+                tmem_ld_wait();
+                const int cb = col0 + c * 32;
+                if (MODE == kModeRaw) {
+                    if (row < P.m) {
+                        int32_t* o = static_cast<int32_t*>(P.out) + ((int64_t)l * P.m + row) * P.n;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (cb + j < P.n) o[cb + j] = (int32_t)v[j];
+                    }
+                } else {
+                    uint32_t w[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        w[q] = pack4(mod_small(v[4 * q], p, mg, sh), mod_small(v[4 * q + 1], p, mg, sh),
+                                     mod_small(v[4 * q + 2], p, mg, sh), mod_small(v[4 * q + 3], p, mg, sh));
+                    if (MODE == kModeResidue) {
                         if (row < P.m) {
-                            int32_t* o = static_cast<int32_t*>(P.out) + ((int64_t)l * P.m + row) * P.n;
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (cb + j < P.n) o[cb + j] = (int32_t)v[j];
-                        }
-                    } else {
-                        uint32_t w[8];
-#pragma unroll
-                        for (int q = 0; q < 8; ++q)
-                            w[q] = pack4(mod_small(v[4 * q], p, mg, sh), mod_small(v[4 * q + 1], p, mg, sh),
-                                         mod_small(v[4 * q + 2], p, mg, sh), mod_small(v[4 * q + 3], p, mg, sh));
-                        if (MODE == kModeResidue) {
-                            if (row < P.m) {
-                                uint8_t* o = static_cast<uint8_t*>(P.out) + ((int64_t)l * P.m + row) * P.n;
+                            uint8_t* o = static_cast<uint8_t*>(P.out) + ((int64_t)l * P.m + row) * P.n;
+                            if (cb + 32 <= P.n && ((reinterpret_cast<uintptr_t>(o + cb) & 15) == 0)) {
+                                reinterpret_cast<uint4*>(o + cb)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                                reinterpret_cast<uint4*>(o + cb)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                            } else {
 #pragma unroll
                                 for (int j = 0; j < 32; ++j)
                                     if (cb + j < P.n) o[cb + j] = (uint8_t)(w[j >> 2] >> (8 * (j & 3)));
                             }
-                        } else {
-                            uint4* d = reinterpret_cast<uint4*>(scr + ((int64_t)l * Cfg::kChunks + c) * 1024);
-                            d[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                            d[1] = make_uint4(w[4], w[5], w[6], w[7]);
                         }
+                    } else {
+                        uint4* d = reinterpret_cast<uint4*>(scr + ((int64_t)l * kChunks + c) * 1024);
+                        d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                        d[1] = make_uint4(w[4], w[5], w[6], w[7]);
                     }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    if constexpr (CG == 1) mbar_arrive(tempty + acc);
-                    else mbar_arrive_cluster(mapa_shared(smem_u32(tempty + acc), 0));
-                }
-                if (++acc == NACC) { acc = 0; aph ^= 1u; }
             }
-            if (!ok) break;
-            if (MODE == kModeCrt && row < P.m) {
-                // CRT for this thread's row segment: kCols columns, 16 at a time,
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if constexpr (CG == 1) mbar_arrive(tempty + acc);
+                else mbar_arrive_cluster(mapa_shared(smem_u32(tempty + acc), 0));
+            }
+            if (++acc == NACC) { acc = 0; aph ^= 1u; }
+
+            if (MODE == kModeCrt && last && row < P.m) {
+                // CRT for this thread's row segment (kCols columns, 16 at a time),
                 // from the residues it staged for every modulus.
                 const int re = P.row_exp[row];
                 double* crow = P.C + row * P.ldc;
 #pragma unroll 1
-                for (int h = 0; h < Cfg::kChunks * 2; ++h) {
+                for (int h = 0; h < kChunks * 2; ++h) {
                     const int cb = col0 + h * 16;
-                    if (cb >= P.n) break;
-                    double hi[16], lo[16];
+                    if (cb < P.n) {
+                        double hi[16], lo[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) { hi[j] = 0.0; lo[j] = 0.0; }
-                    const uint8_t* src = scr + (int64_t)(h >> 1) * 1024 + (h & 1) * 16;
+                        for (int j = 0; j < 16; ++j) { hi[j] = 0.0; lo[j] = 0.0; }
+                        const uint8_t* src = scr + (int64_t)(h >> 1) * 1024 + (h & 1) * 16;
 #pragma unroll 1
-                    for (int l = 0; l < P.n_mod; ++l) {
-                        const uint4 q = *reinterpret_cast<const uint4*>(src + (int64_t)l * Cfg::kChunks * 1024);
-                        const double wh = P.cc.wh[l], wm = P.cc.wm[l], wl = P.cc.wl[l];
-                        const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+                        for (int m2 = 0; m2 < P.n_mod; ++m2) {
+                            const uint4 q = *reinterpret_cast<const uint4*>(src + (int64_t)m2 * kChunks * 1024);
+                            const double wh = P.cc.wh[m2], wm = P.cc.wm[m2], wl = P.cc.wl[m2];
+                            const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                        for (int j = 0; j < 16; ++j)
-                            crt_step((double)((qq[j >> 2] >> (8 * (j & 3))) & 0xFFu), wh, wm, wl, hi[j], lo[j]);
-                    }
+                            for (int j = 0; j < 16; ++j)
+                                crt_step((double)((qq[j >> 2] >> (8 * (j & 3))) & 0xFFu), wh, wm, wl, hi[j], lo[j]);
+                        }
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int col = cb + j;
-                        if (col < P.n)
-                            crow[col] = crt_scale(crt_finish(hi[j], lo[j], P.cc), re, P.col_exp[col], P.two_bits);
+                        for (int j = 0; j < 16; ++j) {
+                            const int col = cb + j;
+                            if (col < P.n)
+                                crow[col] = crt_scale(crt_finish(hi[j], lo[j], P.cc), re, P.col_exp[col], P.two_bits);
+                        }
                     }
                 }
             }
