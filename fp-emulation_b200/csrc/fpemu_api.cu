@@ -278,6 +278,17 @@ int gemm_ctas(const DevInfo& d, int64_t m, int64_t n) {
     return use_pairs() ? 2 * gemm_units<MainCfg>(d, m, n) : gemm_units<SingleCfg>(d, m, n);
 }
 
+// Tile rows per raster band (FPEMU_BAND_ROWS).  Default 8: with 256-row tiles and
+// K = 16384 a band's A strips for one modulus are 32 MB, which stays resident in
+// the L2 while the band's columns stream past; measured on B200 at n = 16384 the
+// GEMM reads 115 GB from DRAM with 8, 138 GB with 16, 240 GB with 32 and 160 GB
+// with 4 (too many B re-reads).
+int band_rows() {
+    const char* s = getenv("FPEMU_BAND_ROWS");
+    const int v = s ? atoi(s) : 8;
+    return v < 1 ? 1 : (v > 1024 ? 1024 : v);
+}
+
 // Schedule of the fused kernel: modulus-major unless FPEMU_GEMM_SCHED=tile.
 int gemm_sched() {
     const char* s = getenv("FPEMU_GEMM_SCHED");
@@ -373,6 +384,7 @@ int launch_gemm_cfg(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int
     P.tiles_m = (int)((m + Cfg::kTileM - 1) / Cfg::kTileM);
     P.tiles_n = (int)((n + Cfg::BN - 1) / Cfg::BN);
     P.num_tiles = P.tiles_m * P.tiles_n;
+    P.band_rows = band_rows();
     P.budget_ns = wait_budget_ns();
     mod_consts(P.n_mod, &P.mc);
     int units = gemm_units<Cfg>(d, m, n);

@@ -61,6 +61,7 @@ struct GemmParams {
     int m, n, k, n_mod;
     int num_kb;            // ceil(k / 128)
     int tiles_m, tiles_n, num_tiles;
+    int band_rows;         // tile rows per raster band
     void* out;             // raw int32 / uint8 residues, [n_mod][m][n] (modes 0, 1)
     double* C;             // mode 2
     int64_t ldc;

@@ -34,7 +34,6 @@ namespace fpemu {
 constexpr int kBM = 128;       // tile rows (TMEM lanes)
 constexpr int kBK = 128;       // K bytes per stage: one 128-byte swizzle row
 constexpr int kUmmaK = 32;     // K of one tcgen05.mma kind::i8
-constexpr int kBandRows = 16;  // tile rows per raster band (L2 reuse of A and B)
 
 template <int CG_, int BN_, int STAGES_, int NEPI_, int NACC_>
 struct GemmCfg {
@@ -64,12 +63,15 @@ struct GemmCfg {
     static int64_t slot_bytes(int n_mod) { return (int64_t)n_mod * kBM * BN; }
 };
 
-__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
-    const int per_band = kBandRows * tiles_n;
+// Band rasterisation: tiles go down `band_rows` tile rows, then to the next
+// column; bands follow each other down the matrix.  Consecutive tiles share
+// A rows (a band's strips stay in L2 while its columns stream past).
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int band_rows, int& tm, int& tn) {
+    const int per_band = band_rows * tiles_n;
     const int band = tile / per_band;
     const int r = tile - band * per_band;
-    const int first = band * kBandRows;
-    const int rows = min(tiles_m - first, kBandRows);
+    const int first = band * band_rows;
+    const int rows = min(tiles_m - first, band_rows);
     tm = first + r % rows;
     tn = r / rows;
 }
@@ -180,7 +182,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     }
                     if (!ok) break;
                 }
-                tile_coords(tile, P.tiles_m, P.tiles_n, tm, tn);
+                tile_coords(tile, P.tiles_m, P.tiles_n, P.band_rows, tm, tn);
                 const int arow = tm * Cfg::kTileM + (int)rank * kBM;
                 const int brow = tn * BN + (int)rank * Cfg::kBRows;
                 for (int kb = 0; kb < P.num_kb; ++kb) {
@@ -283,7 +285,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         for (int idx = 0; ok && idx < my_units; ++idx) {
             int tile, l, tm, tn;
             unit_at(idx, tile, l);
-            tile_coords(tile, P.tiles_m, P.tiles_n, tm, tn);
+            tile_coords(tile, P.tiles_m, P.tiles_n, P.band_rows, tm, tn);
             const int64_t row = (int64_t)tm * Cfg::kTileM + row_in_tile;
             const int col0 = tn * BN + cg * Cfg::kCols;
             uint8_t* scr = nullptr;
