@@ -373,10 +373,10 @@ int launch_split(const SplitParams& P, uint64_t* colmax, const DevInfo& d, cudaS
 }
 
 template <class Cfg, int MODE>
-int launch_gemm_cfg(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int64_t res_ld, const DevInfo& d,
-                    cudaStream_t st, int max_ctas) {
+int launch_gemm_cfg(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int64_t res_ld,
+                    int64_t res_plane_b, const DevInfo& d, cudaStream_t st, int max_ctas) {
     const int64_t m = P.m, n = P.n;
-    const int64_t res_plane_a = m * res_ld, res_plane_b = n * res_ld;
+    const int64_t res_plane_a = m * res_ld;
     CUtensorMap ta, tb;
     FPEMU_TRY(make_residue_map(&ta, a_res, P.k, m, P.n_mod, res_ld, res_plane_a, kBM));
     FPEMU_TRY(make_residue_map(&tb, b_res, P.k, n, P.n_mod, res_ld, res_plane_b, Cfg::kBRows));
@@ -409,11 +409,16 @@ int launch_gemm_cfg(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int
 }
 
 template <int MODE>
-int launch_gemm(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int64_t res_ld, const DevInfo& d,
-                cudaStream_t st, int max_ctas = 0) {
+int launch_gemm(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int64_t res_ld, int64_t res_plane_b,
+                const DevInfo& d, cudaStream_t st, int max_ctas = 0) {
     if (P.m == 0 || P.n == 0) return FPEMU_OK;
-    return use_pairs() ? launch_gemm_cfg<MainCfg, MODE>(P, a_res, b_res, res_ld, d, st, max_ctas)
-                       : launch_gemm_cfg<SingleCfg, MODE>(P, a_res, b_res, res_ld, d, st, max_ctas);
+    if (res_plane_b < (int64_t)P.n * res_ld || res_plane_b % 16 != 0)
+        return fail(FPEMU_ERR_INVALID, "b_res plane stride %lld must be >= n*res_ld and a multiple of 16",
+                    (long long)res_plane_b);
+    if (max_ctas > 0 && max_ctas < 2 && use_pairs())
+        return fail(FPEMU_ERR_INVALID, "max_ctas=%d: the pair GEMM needs at least 2 CTAs", max_ctas);
+    return use_pairs() ? launch_gemm_cfg<MainCfg, MODE>(P, a_res, b_res, res_ld, res_plane_b, d, st, max_ctas)
+                       : launch_gemm_cfg<SingleCfg, MODE>(P, a_res, b_res, res_ld, res_plane_b, d, st, max_ctas);
 }
 
 // ---------------------------------------------- allocation-free staging --
@@ -574,8 +579,8 @@ int fpemu_gemm_residues(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t
     P.n_mod = n_mod;
     P.out = out;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    return mode == 0 ? launch_gemm<kModeRaw>(P, a_res, b_res, res_ld, d, st)
-                     : launch_gemm<kModeResidue>(P, a_res, b_res, res_ld, d, st);
+    return mode == 0 ? launch_gemm<kModeRaw>(P, a_res, b_res, res_ld, n * res_ld, d, st)
+                     : launch_gemm<kModeResidue>(P, a_res, b_res, res_ld, n * res_ld, d, st);
 }
 
 int fpemu_crt_reconstruct(int64_t m, int64_t n, int n_mod, const uint8_t* res, const int32_t* row_exp,
@@ -598,8 +603,8 @@ int fpemu_crt_reconstruct(int64_t m, int64_t n, int n_mod, const uint8_t* res, c
 }
 
 int fpemu_gemm_crt(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_res, const int8_t* b_res,
-                   int64_t res_ld, const int32_t* row_exp, const int32_t* col_exp, int bits, double* C,
-                   int64_t ldc, void* workspace, size_t workspace_bytes, void* stream) {
+                   int64_t res_ld, int64_t b_res_plane, const int32_t* row_exp, const int32_t* col_exp, int bits,
+                   double* C, int64_t ldc, int max_ctas, void* workspace, size_t workspace_bytes, void* stream) {
     DevInfo d;
     FPEMU_TRY(device_info(&d));
     FPEMU_TRY(bits_ok(bits));
@@ -630,7 +635,8 @@ int fpemu_gemm_crt(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_r
         FPEMU_CUDA(cudaMemsetAsync(P.pass_ctr, 0, 256, static_cast<cudaStream_t>(stream)));
     }
     FPEMU_TRY(crt_weights(n_mod, &P.cc));
-    return launch_gemm<kModeCrt>(P, a_res, b_res, res_ld, d, static_cast<cudaStream_t>(stream));
+    return launch_gemm<kModeCrt>(P, a_res, b_res, res_ld, b_res_plane, d, static_cast<cudaStream_t>(stream),
+                                 max_ctas);
 }
 
 int fpemu_gemm_crt_noalloc(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_res,
@@ -669,7 +675,8 @@ int fpemu_gemm_crt_noalloc(int64_t m, int64_t n, int64_t k, int n_mod, const int
     P.sched = kSchedTileMajor;  // one reusable slot per CTA: bounded staging
     FPEMU_TRY(crt_weights(n_mod, &P.cc));
     const int max_ctas = (int)std::min<int64_t>(fit & ~(int64_t)1, 1 << 20);
-    return launch_gemm<kModeCrt>(P, a_res, b_res, res_ld, d, static_cast<cudaStream_t>(stream), max_ctas);
+    return launch_gemm<kModeCrt>(P, a_res, b_res, res_ld, n * res_ld, d, static_cast<cudaStream_t>(stream),
+                                 max_ctas);
 }
 
 int fpemu_ozaki2_dgemm(int64_t m, int64_t n, int64_t k, const double* A, int64_t sA_row, int64_t sA_col,
@@ -700,8 +707,8 @@ int fpemu_ozaki2_dgemm(int64_t m, int64_t n, int64_t k, const double* A, int64_t
     uint64_t* colmax = reinterpret_cast<uint64_t*>(ws + L.colmax);
     FPEMU_TRY(fpemu_split(m, k, A, sA_row, sA_col, bits, n_mod, a_res, L.res_ld, m * L.res_ld, re, colmax, stream));
     FPEMU_TRY(fpemu_split(n, k, B, sB_col, sB_row, bits, n_mod, b_res, L.res_ld, n * L.res_ld, ce, colmax, stream));
-    return fpemu_gemm_crt(m, n, k, n_mod, a_res, b_res, L.res_ld, re, ce, bits, C, ldc, ws + L.scratch,
-                          L.total - L.scratch, stream);
+    return fpemu_gemm_crt(m, n, k, n_mod, a_res, b_res, L.res_ld, n * L.res_ld, re, ce, bits, C, ldc, 0,
+                          ws + L.scratch, L.total - L.scratch, stream);
 }
 
 int fpemu_device_error(int* code, int* where, int* block, int* detail, int clear) {

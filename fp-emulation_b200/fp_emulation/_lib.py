@@ -39,8 +39,8 @@ SIGNATURES = {
     "fpemu_split": (_int, [_i64, _i64, _vp, _i64, _i64, _int, _int, _vp, _i64, _i64, _vp, _vp, _vp]),
     "fpemu_gemm_residues": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _int, _vp, _vp, _sz, _vp]),
     "fpemu_crt_reconstruct": (_int, [_i64, _i64, _int, _vp, _vp, _vp, _int, _vp, _i64, _vp]),
-    "fpemu_gemm_crt": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _vp, _vp, _int, _vp, _i64,
-                              _vp, _sz, _vp]),
+    "fpemu_gemm_crt": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _i64, _vp, _vp, _int, _vp, _i64,
+                              _int, _vp, _sz, _vp]),
     "fpemu_gemm_workspace_size": (_sz, [_i64, _i64, _int]),
     "fpemu_gemm_crt_noalloc": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _vp, _vp, _int, _vp, _i64, _vp]),
     "fpemu_device_error": (_int, [_IP, _IP, _IP, _IP, _int]),

@@ -1,25 +1,39 @@
 """Multi-GPU row-sharded Ozaki-II product: C[rows of this rank] = A_local @ B.
 
 The reference has no multi-GPU code; this is the build's one exchange step.
-A is split by row blocks (each rank holds its own rows; their exponents are
-per row, so no communication), and C is sharded the same way.  B is needed
-whole everywhere: the root rank splits it once into int8 residue planes plus
-column exponents and broadcasts them with NCCL over NVLink.  K is never split,
-so there is no reduction collective.
+A is split by row blocks: each rank holds its own rows, whose exponents are
+per row, so splitting them needs no communication, and C is sharded the same
+way.  B is needed whole everywhere: the root rank splits it into int8 residue
+planes plus column exponents and broadcasts them with NCCL over NVLink.  K is
+never split, so there is no reduction collective.
 
-The broadcast runs on NCCL's stream while this rank splits its own A rows on
-the compute stream; the fused GEMM + CRT kernel starts when both are done.
-One process per GPU (torch.distributed, backend "nccl"; "gloo" works for the
-host-side logic in tests).
+The broadcast is pipelined by column chunks of B.  The root splits chunk c
+and posts its broadcast on NCCL's stream; every rank runs the fused GEMM + CRT
+for chunk c (its rows x the chunk's columns of C) as soon as chunk c has
+arrived, while chunk c+1 is in flight.  The GEMM leaves a few SMs free so
+NCCL's kernels can run next to it.  One process per GPU (torch.distributed,
+backend "nccl").
+
+The orchestration is written against a small backend (`_GpuOps`) so that the
+same pipeline can be exercised with CPU ranks over gloo in tests.
 """
 from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
 
 import torch
 import torch.distributed as dist
 
 from fp_emulation import _lib
 from fp_emulation.ozaki import (_PRECISION_BITS, _after_call, _n_moduli, _require_cuda, _res_ld,
-                                _split, _stream)
+                                _stream)
+
+# Column chunk width of the pipelined broadcast (a multiple of the GEMM's 256-wide tiles).
+CHUNK_COLS = int(os.environ.get("FPEMU_CHUNK_COLS", "2048"))
+# SMs left to NCCL while a chunk's GEMM runs.
+COMM_SMS = int(os.environ.get("FPEMU_COMM_SMS", "16"))
 
 
 def shard_rows(m: int, world: int, rank: int):
@@ -29,35 +43,90 @@ def shard_rows(m: int, world: int, rank: int):
     return r0, r0 + base + (1 if rank < extra else 0)
 
 
-def broadcast_b_residues(B, n: int, k: int, bits: int, n_mod: int, root: int = 0, group=None,
-                         device=None, async_op: bool = False):
-    """Split B ([k, n], on `root`) into residues and broadcast them.
+def plan_column_chunks(n: int, chunk_cols: int = CHUNK_COLS, align: int = 256):
+    """Column ranges [c0, c1) covering [0, n); every chunk but the last is a
+    multiple of `align` wide."""
+    w = max(align, (chunk_cols // align) * align)
+    return [(c0, min(n, c0 + w)) for c0 in range(0, n, w)] or [(0, 0)]
 
-    Returns (b_res int8 [n_mod, n, res_ld], col_exp int32 [n], work) where `work`
-    is the pending broadcast handle when async_op=True (wait() on it before use).
-    Non-root ranks pass B=None.
-    """
+
+@dataclass
+class _Chunk:
+    c0: int
+    c1: int
+    res: torch.Tensor      # int8 [n_mod, c1 - c0, ld] (contiguous: one broadcast)
+    work: object = None
+
+
+class _GpuOps:
+    """The product backend: libfpemu through the C ABI on the current stream."""
+
+    def __init__(self, device, timing=None):
+        self.device = device
+        self.lib = _lib.load()
+        props = torch.cuda.get_device_properties(device)
+        self.max_ctas = max(2, props.multi_processor_count - COMM_SMS)
+        self.timing = timing  # optional list collecting (start, end, int8_ops) per GEMM launch
+
+    def empty_res(self, n_mod, rows, ld):
+        return torch.empty((n_mod, rows, ld), dtype=torch.int8, device=self.device)
+
+    def empty_exps(self, rows):
+        return torch.empty((rows,), dtype=torch.int32, device=self.device)
+
+    def split(self, X, bits, n_mod, res, exps):
+        """Residues of the rows of X [rows, k] into res [n_mod, rows, ld], exponents into exps."""
+        rows, k = X.shape
+        ld = res.shape[2]
+        colmax = torch.empty((max(rows, 1),), dtype=torch.int64, device=self.device) if X.stride(1) != 1 else None
+        st = self.lib.fpemu_split(rows, k, X.data_ptr(), X.stride(0), X.stride(1), bits, n_mod, res.data_ptr(),
+                                  ld, res.stride(0), exps.data_ptr(),
+                                  None if colmax is None else colmax.data_ptr(), _stream(self.device))
+        _lib.check(st, "split")
+
+    def gemm_crt(self, a_res, re, b_res, ce, bits, C, c0, c1, k):
+        n_mod, m, ld = a_res.shape
+        w = c1 - c0
+        nbytes = self.lib.fpemu_gemm_workspace_size(m, w, n_mod)
+        ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=self.device)
+        Cv = C[:, c0:c1]
+        if self.timing is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        st = self.lib.fpemu_gemm_crt(m, w, k, n_mod, a_res.data_ptr(), b_res.data_ptr(), ld, b_res.stride(0),
+                                     re.data_ptr(), ce[c0:c1].data_ptr(), bits, Cv.data_ptr(), C.stride(0),
+                                     self.max_ctas, ws.data_ptr(), ws.numel(), _stream(self.device))
+        _lib.check(st, "gemm_crt")
+        if self.timing is not None:
+            ev[1].record()
+            self.timing.append((ev[0], ev[1], 2.0 * m * w * k * n_mod))
+
+
+def rowsharded_product(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, chunk_cols=CHUNK_COLS):
+    """The pipeline: chunked split/broadcast of B's residues, split of A's rows,
+    one fused GEMM per chunk.  Returns C_local [m_local, n] (float64)."""
     rank = dist.get_rank(group)
-    dev = device if device is not None else (B.device if B is not None else torch.device("cuda"))
-    if rank == root:
-        _require_cuda(B)
-        b_res, col_exp = _split(B.T, bits, n_mod)
-    else:
-        b_res = torch.empty((n_mod, n, _res_ld(k)), dtype=torch.int8, device=dev)
-        col_exp = torch.empty((n,), dtype=torch.int32, device=dev)
-    w1 = dist.broadcast(b_res, src=root, group=group, async_op=True)
-    w2 = dist.broadcast(col_exp, src=root, group=group, async_op=True)
-
-    class _Both:
-        def wait(self):
-            w1.wait()
-            w2.wait()
-
-    work = _Both()
-    if not async_op:
-        work.wait()
-        return b_res, col_exp, None
-    return b_res, col_exp, work
+    m = A_local.shape[0]
+    ld = _res_ld(k)
+    col_exp = ops.empty_exps(n)
+    chunks = []
+    for c0, c1 in plan_column_chunks(n, chunk_cols):
+        ch = _Chunk(c0, c1, ops.empty_res(n_mod, c1 - c0, ld))
+        if rank == root:
+            ops.split(B[:, c0:c1].T, bits, n_mod, ch.res, col_exp[c0:c1])
+        ch.work = dist.broadcast(ch.res, src=root, group=group, async_op=True)
+        chunks.append(ch)
+    exp_work = dist.broadcast(col_exp, src=root, group=group, async_op=True)
+    a_res = ops.empty_res(n_mod, m, ld)
+    row_exp = ops.empty_exps(m)
+    ops.split(A_local, bits, n_mod, a_res, row_exp)   # overlaps the broadcasts
+    C = torch.empty((m, n), dtype=torch.float64, device=A_local.device)
+    exp_work.wait()
+    for ch in chunks:
+        ch.work.wait()                                  # this chunk has arrived
+        if m and ch.c1 > ch.c0:
+            ops.gemm_crt(a_res, row_exp, ch.res, col_exp, bits, C, ch.c0, ch.c1, k)
+    return C
 
 
 def ozaki2_int8_matmul_rowsharded(A_local, B, n: int | None = None, root: int = 0, group=None):
@@ -73,28 +142,19 @@ def ozaki2_int8_matmul_rowsharded(A_local, B, n: int | None = None, root: int = 
     dev = _require_cuda(A_local)
     orig = A_local.dtype
     A_local = A_local.double()
-    m, k = A_local.shape
-    rank = dist.get_rank(group)
-    if rank == root:
-        if B is None or B.shape[0] != k:
+    k = A_local.shape[1]
+    if dist.get_rank(group) == root:
+        if B is None or B.dim() != 2 or B.shape[0] != k:
             raise RuntimeError("root must pass B with B.shape[0] == A_local.shape[1]")
+        _require_cuda(B)
         B = B.double()
         n = B.shape[1]
     if n is None:
         raise RuntimeError("non-root ranks must pass n (B's column count)")
+    if k == 0:
+        raise RuntimeError("inner dimension k must be non-zero")
     n_mod = _n_moduli(k, bits)
-    b_res, col_exp, work = broadcast_b_residues(B, n, k, bits, n_mod, root, group, dev, async_op=True)
-    a_res, row_exp = _split(A_local, bits, n_mod)   # overlaps the broadcast
-    work.wait()
-    C = torch.empty((m, n), dtype=torch.float64, device=dev)
-    if m and n:
-        lib = _lib.load()
-        nbytes = lib.fpemu_gemm_workspace_size(m, n, n_mod)
-        ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=dev)
-        with torch.cuda.device(dev):
-            st = lib.fpemu_gemm_crt(m, n, k, n_mod, a_res.data_ptr(), b_res.data_ptr(), _res_ld(k),
-                                    row_exp.data_ptr(), col_exp.data_ptr(), bits, C.data_ptr(), n,
-                                    ws.data_ptr(), ws.numel(), _stream(dev))
-        _lib.check(st, "ozaki2_int8_matmul_rowsharded")
-        _after_call("ozaki2_int8_matmul_rowsharded")
+    with torch.cuda.device(dev):
+        C = rowsharded_product(A_local, B, n, k, bits, n_mod, _GpuOps(dev), root, group)
+    _after_call("ozaki2_int8_matmul_rowsharded")
     return C if orig == torch.float64 else C.to(orig)

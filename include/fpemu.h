@@ -113,12 +113,16 @@ int fpemu_crt_reconstruct(int64_t m, int64_t n, int n_mod, const uint8_t *res,
                           int64_t ldc, void *stream);
 
 /* The fused GEMM + mod + CRT stage on residues that are already split
- * (crt_kernel.cu:19-146 in one kernel).  The multi-GPU driver calls this after
- * B's residues arrive by broadcast. */
+ * (crt_kernel.cu:19-146 in one kernel).  b_res_plane is the plane stride of
+ * b_res (n * res_ld when the planes are packed; larger for a column chunk of a
+ * bigger residue buffer).  max_ctas > 0 caps the persistent grid (the
+ * multi-GPU driver leaves SMs free for NCCL's kernels); 0 uses every SM.  The
+ * multi-GPU driver calls this per column chunk of B as its residues arrive. */
 int fpemu_gemm_crt(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t *a_res,
-                   const int8_t *b_res, int64_t res_ld, const int32_t *row_exp,
-                   const int32_t *col_exp, int bits, double *C, int64_t ldc, void *workspace,
-                   size_t workspace_bytes, void *stream);
+                   const int8_t *b_res, int64_t res_ld, int64_t b_res_plane,
+                   const int32_t *row_exp, const int32_t *col_exp, int bits, double *C,
+                   int64_t ldc, int max_ctas, void *workspace, size_t workspace_bytes,
+                   void *stream);
 
 /* Allocation-free variant of fpemu_gemm_crt.  It has no counterpart in the
  * reference.  For callers that cannot allocate device memory -- code running

@@ -48,8 +48,9 @@ def _run_both(torch, lib, A_np, B_np):
     # Regular entry point: caller-provided workspace.
     C_ref = torch.full((m, n), float("nan"), dtype=torch.float64, device=dev)
     ws = torch.empty((lib.fpemu_gemm_workspace_size(m, n, n_mod),), dtype=torch.uint8, device=dev)
-    _lib.check(lib.fpemu_gemm_crt(m, n, k, n_mod, a_res.data_ptr(), b_res.data_ptr(), ld, re.data_ptr(),
-                                  ce.data_ptr(), 53, C_ref.data_ptr(), n, ws.data_ptr(), ws.numel(), stream),
+    _lib.check(lib.fpemu_gemm_crt(m, n, k, n_mod, a_res.data_ptr(), b_res.data_ptr(), ld, n * ld,
+                                  re.data_ptr(), ce.data_ptr(), 53, C_ref.data_ptr(), n, 0, ws.data_ptr(),
+                                  ws.numel(), stream),
                "fpemu_gemm_crt")
 
     # Allocation-free entry point: inputs and output only.
