@@ -34,6 +34,10 @@ from fp_emulation.ozaki import (_PRECISION_BITS, _after_call, _n_moduli, _requir
 CHUNK_COLS = int(os.environ.get("FPEMU_CHUNK_COLS", "2048"))
 # SMs left to NCCL while a chunk's GEMM runs.
 COMM_SMS = int(os.environ.get("FPEMU_COMM_SMS", "16"))
+# What the root broadcasts: "residues" (B's int8 residue planes, n_mod bytes per
+# element, the default) or "fp64" (B itself, 8 bytes per element; every rank then
+# splits the chunk locally -- less NVLink traffic for more split work per rank).
+BCAST_MODE = os.environ.get("FPEMU_BCAST", "residues")
 
 
 def shard_rows(m: int, world: int, rank: int):
@@ -56,6 +60,7 @@ class _Chunk:
     c1: int
     res: torch.Tensor      # int8 [n_mod, c1 - c0, ld] (contiguous: one broadcast)
     work: object = None
+    fp64: torch.Tensor = None  # mode "fp64": the chunk of B, [k, c1 - c0]
 
 
 class _GpuOps:
@@ -102,9 +107,14 @@ class _GpuOps:
             self.timing.append((ev[0], ev[1], 2.0 * m * w * k * n_mod))
 
 
-def rowsharded_product(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, chunk_cols=CHUNK_COLS):
-    """The pipeline: chunked split/broadcast of B's residues, split of A's rows,
-    one fused GEMM per chunk.  Returns C_local [m_local, n] (float64)."""
+def rowsharded_product(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, chunk_cols=CHUNK_COLS,
+                       mode=None):
+    """The pipeline: chunked split/broadcast of B's residues (or of B itself,
+    mode "fp64"), split of A's rows, one fused GEMM per chunk.  Returns C_local
+    [m_local, n] (float64)."""
+    mode = mode or BCAST_MODE
+    if mode not in ("residues", "fp64"):
+        raise ValueError(f"broadcast mode {mode!r}")
     rank = dist.get_rank(group)
     m = A_local.shape[0]
     ld = _res_ld(k)
@@ -112,18 +122,31 @@ def rowsharded_product(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, c
     chunks = []
     for c0, c1 in plan_column_chunks(n, chunk_cols):
         ch = _Chunk(c0, c1, ops.empty_res(n_mod, c1 - c0, ld))
-        if rank == root:
-            ops.split(B[:, c0:c1].T, bits, n_mod, ch.res, col_exp[c0:c1])
-        ch.work = dist.broadcast(ch.res, src=root, group=group, async_op=True)
+        if mode == "residues":
+            if rank == root:
+                ops.split(B[:, c0:c1].T, bits, n_mod, ch.res, col_exp[c0:c1])
+            ch.work = dist.broadcast(ch.res, src=root, group=group, async_op=True)
+        else:
+            ch.fp64 = (B[:, c0:c1].contiguous() if rank == root
+                       else torch.empty((k, c1 - c0), dtype=torch.float64, device=A_local.device))
+            ch.work = dist.broadcast(ch.fp64, src=root, group=group, async_op=True)
         chunks.append(ch)
-    exp_work = dist.broadcast(col_exp, src=root, group=group, async_op=True)
+    exp_work = (dist.broadcast(col_exp, src=root, group=group, async_op=True) if mode == "residues" else None)
     a_res = ops.empty_res(n_mod, m, ld)
     row_exp = ops.empty_exps(m)
     ops.split(A_local, bits, n_mod, a_res, row_exp)   # overlaps the broadcasts
     C = torch.empty((m, n), dtype=torch.float64, device=A_local.device)
-    exp_work.wait()
+    if exp_work is not None:
+        exp_work.wait()
+    if mode == "fp64":
+        # Split every chunk as it lands (short kernels that interleave with NCCL's
+        # CTAs), then run the GEMMs on all SMs.
+        for ch in chunks:
+            ch.work.wait()
+            ops.split(ch.fp64.T, bits, n_mod, ch.res, col_exp[ch.c0:ch.c1])
     for ch in chunks:
-        ch.work.wait()                                  # this chunk has arrived
+        if mode == "residues":
+            ch.work.wait()                              # this chunk has arrived
         if m and ch.c1 > ch.c0:
             ops.gemm_crt(a_res, row_exp, ch.res, col_exp, bits, C, ch.c0, ch.c1, k)
     return C

@@ -55,7 +55,7 @@ class OracleOps:
         C[:, c0:c1] = torch.from_numpy(oo.reconstruct(res, moduli, bits, re.numpy(), ce[c0:c1].numpy()))
 
 
-def _worker(rank, world, port, m, k, n, chunk_cols, out_q, drop_rank):
+def _worker(rank, world, port, m, k, n, chunk_cols, out_q, drop_rank, mode="residues"):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         torch.distributed.init_process_group("gloo", rank=rank, world_size=world,
@@ -71,18 +71,18 @@ def _worker(rank, world, port, m, k, n, chunk_cols, out_q, drop_rank):
             return  # leaves between steps, before any collective
         n_mod = oo.n_moduli(k, 53)
         C = rowsharded_product(torch.from_numpy(A[r0:r1]), torch.from_numpy(B) if rank == 0 else None,
-                               n, k, 53, n_mod, OracleOps(), root=0, chunk_cols=chunk_cols)
+                               n, k, 53, n_mod, OracleOps(), root=0, chunk_cols=chunk_cols, mode=mode)
         out_q.put((rank, "ok", (r0, r1, C.numpy())))
         torch.distributed.destroy_process_group()
     except Exception:
         out_q.put((rank, "error", traceback.format_exc()))
 
 
-def _run(world, m, k, n, chunk_cols, drop_rank=-1, wait=120):
+def _run(world, m, k, n, chunk_cols, drop_rank=-1, wait=120, mode="residues"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, m, k, n, chunk_cols, q, drop_rank))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, m, k, n, chunk_cols, q, drop_rank, mode))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -94,9 +94,10 @@ def _run(world, m, k, n, chunk_cols, drop_rank=-1, wait=120):
     return results
 
 
+@pytest.mark.parametrize("mode", ["residues", "fp64"])
 @pytest.mark.parametrize("m,k,n,chunk", [(37, 90, 300, 256), (64, 300, 520, 512)])
-def test_rowsharded_pipeline_matches_oracle(m, k, n, chunk):
-    results = _run(2, m, k, n, chunk)
+def test_rowsharded_pipeline_matches_oracle(m, k, n, chunk, mode):
+    results = _run(2, m, k, n, chunk, mode=mode)
     C = np.full((m, n), np.nan)
     for rank, status, payload in results:
         assert status == "ok", payload
