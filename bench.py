@@ -302,10 +302,17 @@ def run_ours(args):
                   "step_rank0": round(statistics.mean(e[0].elapsed_time(e[1]) for e in n_steps_events), 3)}
     achieved = int8_ops / (gemm_ms * 1e-3) / 1e12
     peaks = measured_peaks()
+    # MEASURED_PEAKS.json has no INT8 figure; B200's dense INT8 rate is twice its dense
+    # BF16 rate, so the denominators are 2x the measured cuBLAS bf16 rates.  The
+    # kernel runs inside a seconds-long loop, so the sustained figure is the
+    # primary one; INT8 tensor work draws less power per op than bf16 and holds a
+    # higher clock under the 1 kW cap, so the burst figure is reported beside it.
     if peaks.get("bf16_tflops_sustained"):
-        peak, peak_src = 2.0 * peaks["bf16_tflops_sustained"], "2 x bf16_tflops_sustained of measured (INT8 dense = 2 x BF16 dense)"
+        peak, peak_src = 2.0 * peaks["bf16_tflops_sustained"], "2 x bf16_tflops_sustained of measured"
+        peak_burst = 2.0 * peaks.get("bf16_tflops", peaks["bf16_tflops_sustained"])
     else:
-        peak, peak_src = 2.0 * 1590.0, "2 x 1.59 PFLOP/s bf16 of fallback"
+        peak, peak_src = 2.0 * 1400.0, "2 x 1.4 PFLOP/s sustained bf16 of fallback"
+        peak_burst = 2.0 * 1590.0
     # Our kernels per step: split A (1), split B on the root (column max + split: 2 per
     # chunk), one GEMM per chunk (1 chunk on a single GPU).
     nch = 1 if world == 1 else n_chunks
@@ -405,9 +412,10 @@ def run_ours(args):
             "roofline": {"bound": "tensor", "kernel": "ozaki_gemm_kernel (fused INT8 GEMM + mod + CRT)",
                          "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                         "peak_burst": round(peak_burst, 1), "frac_burst": round(achieved / peak_burst, 4),
                          "ops_per_launch": int8_ops, "launch_ms": round(gemm_ms, 3),
                          "traffic": gemm_traffic_per_launch(n)},
-            "int8_tc_util": round(achieved / peak, 4),
+            "int8_tc_util": round(achieved / peak_burst, 4),
             "stages_ms": stages,
             "gpu_launches": launches,
             "clocks": clk.summary(),

@@ -271,7 +271,7 @@ def test_nonfinite_rows_give_nan(torch_cuda):
 
 @pytest.mark.parametrize("sched", ["modulus", "tile"])
 @pytest.mark.parametrize("ctas", ["1", "2"])
-@pytest.mark.parametrize("m,k,n", [(300, 520, 700), (513, 1100, 257), (1000, 300, 1000)])
+@pytest.mark.parametrize("m,k,n", [(300, 520, 700), (513, 1100, 257), (1000, 300, 1000), (2600, 200, 700)])
 def test_gemm_configurations_agree(torch_cuda, monkeypatch, sched, ctas, m, k, n):
     """The CTA-pair GEMM (default) and the single-CTA GEMM (FPEMU_GEMM_CTAS=1),
     each with the modulus-major (default) and the tile-major
