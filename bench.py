@@ -61,7 +61,9 @@ def workload_config(n, phi, n_mod, world):
         "workload": f"BASELINE config 2 point n={n}: square FP64 GEMM, entries (U(0,1)-0.5)*exp({phi}*N(0,1))",
         "m": n, "n": n, "k": n, "n_mod": n_mod, "phi": phi,
         "l2": "inputs larger than L2 (2 GiB per operand); no flush",
-        "parallelism": "single GPU" if world == 1 else f"A row-sharded over {world} GPUs, B residues NCCL-broadcast",
+        "parallelism": "single GPU" if world == 1 else (
+            f"A row-sharded over {world} GPUs, B residues broadcast over NVLink "
+            f"({os.environ.get('FPEMU_TRANSPORT', 'ce')} transport, {os.environ.get('FPEMU_BCAST', 'residues')})"),
     }
 
 
@@ -206,16 +208,18 @@ def run_ours(args):
     gemm_timing = []
     dist_ops = None
     if world > 1:
-        from fp_emulation.distributed import _GpuOps, plan_column_chunks, rowsharded_product
+        import fp_emulation.distributed as fdist
 
-        dist_ops = _GpuOps(dev)
-        n_chunks = len(plan_column_chunks(n))
+        use_ce = fdist.BCAST_MODE == "residues" and fdist.TRANSPORT == "ce"
+        dist_ops = fdist._GpuOps(dev, comm_sms=0 if use_ce else None)
+        n_chunks = len(fdist.plan_column_chunks(n))
+        product = fdist.rowsharded_product_ce if use_ce else fdist.rowsharded_product
 
     def step_dist(record):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)] if record else None
         dist_ops.timing = gemm_timing if record else None
         if ev: ev[0].record(stream)
-        rowsharded_product(A, B, n, k, bits, n_mod, dist_ops, root=root)
+        product(A, B, n, k, bits, n_mod, dist_ops, root=root)
         if ev:
             ev[1].record(stream)
             n_steps_events.append(ev)

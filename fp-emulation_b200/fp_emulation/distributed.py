@@ -38,6 +38,9 @@ COMM_SMS = int(os.environ.get("FPEMU_COMM_SMS", "16"))
 # element, the default) or "fp64" (B itself, 8 bytes per element; every rank then
 # splits the chunk locally -- less NVLink traffic for more split work per rank).
 BCAST_MODE = os.environ.get("FPEMU_BCAST", "residues")
+# How residues travel: "ce" (copy-engine chain over NVLink through CUDA IPC, no SMs;
+# see ce_chain.py) or "nccl" (NCCL broadcast kernels).
+TRANSPORT = os.environ.get("FPEMU_TRANSPORT", "ce")
 
 
 def shard_rows(m: int, world: int, rank: int):
@@ -66,11 +69,12 @@ class _Chunk:
 class _GpuOps:
     """The product backend: libfpemu through the C ABI on the current stream."""
 
-    def __init__(self, device, timing=None):
+    def __init__(self, device, timing=None, comm_sms=None):
         self.device = device
         self.lib = _lib.load()
         props = torch.cuda.get_device_properties(device)
-        self.max_ctas = max(2, props.multi_processor_count - COMM_SMS)
+        spare = COMM_SMS if comm_sms is None else comm_sms
+        self.max_ctas = 0 if spare <= 0 else max(2, props.multi_processor_count - spare)
         self.timing = timing  # optional list collecting (start, end, int8_ops) per GEMM launch
 
     def empty_res(self, n_mod, rows, ld):
@@ -89,7 +93,9 @@ class _GpuOps:
                                   None if colmax is None else colmax.data_ptr(), _stream(self.device))
         _lib.check(st, "split")
 
-    def gemm_crt(self, a_res, re, b_res, ce, bits, C, c0, c1, k):
+    def gemm_crt(self, a_res, re, b_res, ce_chunk, bits, C, c0, c1, k):
+        """C[:, c0:c1] from A's residues and one column chunk of B's (ce_chunk: that
+        chunk's column exponents)."""
         n_mod, m, ld = a_res.shape
         w = c1 - c0
         nbytes = self.lib.fpemu_gemm_workspace_size(m, w, n_mod)
@@ -99,7 +105,7 @@ class _GpuOps:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
         st = self.lib.fpemu_gemm_crt(m, w, k, n_mod, a_res.data_ptr(), b_res.data_ptr(), ld, b_res.stride(0),
-                                     re.data_ptr(), ce[c0:c1].data_ptr(), bits, Cv.data_ptr(), C.stride(0),
+                                     re.data_ptr(), ce_chunk.data_ptr(), bits, Cv.data_ptr(), C.stride(0),
                                      self.max_ctas, ws.data_ptr(), ws.numel(), _stream(self.device))
         _lib.check(st, "gemm_crt")
         if self.timing is not None:
@@ -148,7 +154,61 @@ def rowsharded_product(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, c
         if mode == "residues":
             ch.work.wait()                              # this chunk has arrived
         if m and ch.c1 > ch.c0:
-            ops.gemm_crt(a_res, row_exp, ch.res, col_exp, bits, C, ch.c0, ch.c1, k)
+            ops.gemm_crt(a_res, row_exp, ch.res, col_exp[ch.c0:ch.c1], bits, C, ch.c0, ch.c1, k)
+    return C
+
+
+_CHAINS = {}
+
+
+def _align256(x):
+    return (x + 255) // 256 * 256
+
+
+def rowsharded_product_ce(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, chunk_cols=CHUNK_COLS):
+    """Same product, B's residues moved by the copy-engine chain (ce_chain.py): the
+    root splits each column chunk straight into its shared buffer, every other rank
+    pulls the chunk piece by piece from its predecessor, and each rank's GEMM on
+    chunk c starts when chunk c has landed -- no SMs spent on the transfer."""
+    from fp_emulation.ce_chain import CeChain
+
+    rank = dist.get_rank(group)
+    dev = A_local.device
+    m = A_local.shape[0]
+    ld = _res_ld(k)
+    plan = plan_column_chunks(n, chunk_cols)
+    wmax = max(c1 - c0 for c0, c1 in plan)
+    res_bytes = _align256(n_mod * wmax * ld)
+    chunk_bytes = res_bytes + _align256(wmax * 4)
+    key = (id(group), root, dev.index, chunk_bytes, len(plan))
+    chain = _CHAINS.get(key)
+    if chain is None:
+        chain = _CHAINS[key] = CeChain(group, root, dev, chunk_bytes, len(plan))
+    stream = torch.cuda.current_stream(dev)
+    chain.begin()
+    views = []
+    for c, (c0, c1) in enumerate(plan):
+        w = c1 - c0
+        blk = chain.chunk_view(c)
+        res = blk[: n_mod * w * ld].view(n_mod, w, ld)
+        exps = blk[res_bytes: res_bytes + 4 * w].view(torch.int32)
+        if rank == root:
+            chain.root_before_write(c, stream)
+            ops.split(B[:, c0:c1].T, bits, n_mod, res, exps)
+            chain.root_after_write(c, stream)
+        views.append((c0, c1, res, exps))
+    if rank != root:
+        chain.relay()
+    chain.publish()
+    a_res = ops.empty_res(n_mod, m, ld)
+    row_exp = ops.empty_exps(m)
+    ops.split(A_local, bits, n_mod, a_res, row_exp)
+    C = torch.empty((m, n), dtype=torch.float64, device=dev)
+    for c, (c0, c1, res, exps) in enumerate(views):
+        chain.wait_chunk(c, stream)
+        if m and c1 > c0:
+            ops.gemm_crt(a_res, row_exp, res, exps, bits, C, c0, c1, k)
+        chain.after_gemm(c, stream)
     return C
 
 
@@ -178,6 +238,9 @@ def ozaki2_int8_matmul_rowsharded(A_local, B, n: int | None = None, root: int = 
         raise RuntimeError("inner dimension k must be non-zero")
     n_mod = _n_moduli(k, bits)
     with torch.cuda.device(dev):
-        C = rowsharded_product(A_local, B, n, k, bits, n_mod, _GpuOps(dev), root, group)
+        if BCAST_MODE == "residues" and TRANSPORT == "ce":
+            C = rowsharded_product_ce(A_local, B, n, k, bits, n_mod, _GpuOps(dev, comm_sms=0), root, group)
+        else:
+            C = rowsharded_product(A_local, B, n, k, bits, n_mod, _GpuOps(dev), root, group)
     _after_call("ozaki2_int8_matmul_rowsharded")
     return C if orig == torch.float64 else C.to(orig)

@@ -46,13 +46,13 @@ class OracleOps:
         res[:, :, :k] = torch.from_numpy(oo.residues(A_int, oo.PRIMES[:n_mod]))
         exps.copy_(torch.from_numpy(re))
 
-    def gemm_crt(self, a_res, re, b_res, ce, bits, C, c0, c1, k):
+    def gemm_crt(self, a_res, re, b_res, ce_chunk, bits, C, c0, c1, k):
         n_mod = a_res.shape[0]
         moduli = oo.PRIMES[:n_mod]
         a = a_res[:, :, :k].numpy()
         b = b_res[:, :, :k].numpy().transpose(0, 2, 1)
         res = oo.matmul_residues(a, b, moduli)
-        C[:, c0:c1] = torch.from_numpy(oo.reconstruct(res, moduli, bits, re.numpy(), ce[c0:c1].numpy()))
+        C[:, c0:c1] = torch.from_numpy(oo.reconstruct(res, moduli, bits, re.numpy(), ce_chunk.numpy()))
 
 
 def _worker(rank, world, port, m, k, n, chunk_cols, out_q, drop_rank, mode="residues"):

@@ -30,12 +30,12 @@ def _problem(m, k, n):
     return A, B
 
 
-def _worker(rank, world, port, m, k, n, q):
+def _worker(rank, world, port, m, k, n, q, transport="ce", calls=2):
     try:
         import torch
 
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
-                          FPEMU_CHUNK_COLS="512")
+                          FPEMU_CHUNK_COLS="512", FPEMU_TRANSPORT=transport)
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
         torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
@@ -47,7 +47,9 @@ def _worker(rank, world, port, m, k, n, q):
         r0, r1 = shard_rows(m, world, rank)
         A_local = torch.from_numpy(A[r0:r1]).to(dev)
         B_t = torch.from_numpy(B).to(dev) if rank == 0 else None
-        C = ozaki2_int8_matmul_rowsharded(A_local, B_t, n=n, root=0)
+        # Several calls in a row: buffers and events of the transport are reused.
+        for _ in range(calls):
+            C = ozaki2_int8_matmul_rowsharded(A_local, B_t, n=n, root=0)
         torch.cuda.synchronize(dev)
         code = _lib.device_error(clear=True)
         q.put((rank, "ok", (r0, r1, C.cpu().numpy(), code)))
@@ -57,7 +59,8 @@ def _worker(rank, world, port, m, k, n, q):
         q.put((rank, "error", traceback.format_exc()))
 
 
-def test_rowsharded_two_gpus_bit_exact():
+@pytest.mark.parametrize("transport", ["ce", "nccl"])
+def test_rowsharded_two_gpus_bit_exact(transport):
     import torch
     import torch.multiprocessing as mp
 
@@ -67,7 +70,7 @@ def test_rowsharded_two_gpus_bit_exact():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, m, k, n, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, m, k, n, q, transport)) for r in range(2)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in range(2)]
