@@ -63,7 +63,7 @@ def workload_config(n, phi, n_mod, world):
         "l2": "inputs larger than L2 (2 GiB per operand); no flush",
         "parallelism": "single GPU" if world == 1 else (
             f"A row-sharded over {world} GPUs, B residues broadcast over NVLink "
-            f"({os.environ.get('FPEMU_TRANSPORT', 'ce')} transport, {os.environ.get('FPEMU_BCAST', 'residues')})"),
+            f"({os.environ.get('FPEMU_TRANSPORT', 'nvls')} transport, {os.environ.get('FPEMU_BCAST', 'residues')})"),
     }
 
 
@@ -210,10 +210,10 @@ def run_ours(args):
     if world > 1:
         import fp_emulation.distributed as fdist
 
-        use_ce = fdist.BCAST_MODE == "residues" and fdist.TRANSPORT == "ce"
+        use_ce = fdist.BCAST_MODE == "residues" and fdist.TRANSPORT != "nccl"
         dist_ops = fdist._GpuOps(dev, comm_sms=0 if use_ce else None)
         n_chunks = len(fdist.plan_column_chunks(n))
-        product = fdist.rowsharded_product_ce if use_ce else fdist.rowsharded_product
+        product = fdist.rowsharded_product_auto
 
     def step_dist(record):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)] if record else None

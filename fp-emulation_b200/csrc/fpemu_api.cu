@@ -257,7 +257,10 @@ int max_active_units(const DevInfo& d) {
     return clusters;
 }
 
-// Launch units (CTAs, or CTA pairs) for an m x n problem; cached per device.
+// Launch units (CTAs, or CTA pairs) for an m x n problem (capacity cached per
+// device): the fewest units that still finish the tiles in the fewest waves, so
+// 64 tiles take 64 pairs rather than 74 (no slower: every unit does one tile per
+// pass either way) and leave SMs free for kernels on other streams.
 template <class Cfg>
 int gemm_units(const DevInfo& d, int64_t m, int64_t n) {
     static std::mutex mu;
@@ -271,7 +274,9 @@ int gemm_units(const DevInfo& d, int64_t m, int64_t n) {
         cap = cache[dev & 63];
     }
     const int64_t tiles = ((m + Cfg::kTileM - 1) / Cfg::kTileM) * ((n + Cfg::BN - 1) / Cfg::BN);
-    return (int)(tiles < cap ? tiles : cap);
+    if (cap <= 0 || tiles <= 0) return 0;
+    const int64_t waves = (tiles + cap - 1) / cap;
+    return (int)((tiles + waves - 1) / waves);
 }
 
 int gemm_ctas(const DevInfo& d, int64_t m, int64_t n) {
@@ -366,7 +371,7 @@ int launch_split(const SplitParams& P, uint64_t* colmax, const DevInfo& d, cudaS
         SplitParams Q = P;
         Q.colmax = colmax;
         dim3 g2((unsigned)((P.rows + kTileR - 1) / kTileR), (unsigned)((P.res_ld + kTileK - 1) / kTileK));
-        split_strided_kernel<<<g2, 256, 0, st>>>(Q);
+        split_strided_kernel<false><<<g2, 256, 0, st>>>(Q);
     }
     FPEMU_CUDA(cudaGetLastError());
     return FPEMU_OK;
@@ -559,6 +564,85 @@ int fpemu_split(int64_t rows, int64_t k, const double* X, int64_t s_row, int64_t
     P.n_mod = n_mod;
     mod_consts(n_mod, &P.mc);
     return launch_split(P, colmax_scratch, d, static_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------- multi-GPU (NVLS) primitives --
+
+int64_t fpemu_split_mc_signals(int64_t rows, int64_t k) {
+    if (rows <= 0 || k < 1) return 0;
+    const int64_t res_ld = res_ld_for(k);
+    return ((rows + kTileR - 1) / kTileR) * ((res_ld + kTileK - 1) / kTileK);
+}
+
+int fpemu_split_mc(int64_t rows, int64_t k, const double* X, int64_t s_row, int64_t s_k, int bits, int n_mod,
+                   int8_t* res_mc, int64_t res_ld, int64_t res_plane, int32_t* exps_mc, uint64_t* colmax_scratch,
+                   uint64_t* done_mc, void* stream) {
+    DevInfo d;
+    FPEMU_TRY(device_info(&d));
+    FPEMU_TRY(bits_ok(bits));
+    if (rows < 0 || k < 1 || s_row < 0 || s_k < 0) return fail(FPEMU_ERR_INVALID, "split_mc: bad sizes or strides");
+    if (s_k == 1) return fail(FPEMU_ERR_UNSUPPORTED, "split_mc: only strided K (s_k != 1) is supported");
+    if (n_mod < 1 || n_mod > kMaxModuli) return fail(FPEMU_ERR_UNSUPPORTED, "n_mod=%d outside [1, %d]", n_mod, kMaxModuli);
+    if (res_ld != res_ld_for(k) || res_plane < rows * res_ld || res_plane % 16 != 0)
+        return fail(FPEMU_ERR_INVALID, "split_mc: res_ld must be %lld and res_plane >= rows*res_ld, a multiple of 16",
+                    (long long)res_ld_for(k));
+    if (rows == 0) return FPEMU_OK;
+    if (!X || !res_mc || !exps_mc || !colmax_scratch || !done_mc) return fail(FPEMU_ERR_INVALID, "split_mc: null pointer");
+    if (reinterpret_cast<uintptr_t>(res_mc) % 16 != 0 || reinterpret_cast<uintptr_t>(exps_mc) % 4 != 0 ||
+        reinterpret_cast<uintptr_t>(done_mc) % 8 != 0)
+        return fail(FPEMU_ERR_INVALID, "split_mc: misaligned res (16), exps (4) or counter (8)");
+    SplitParams P;
+    memset(&P, 0, sizeof P);
+    P.X = X;
+    P.rows = rows;
+    P.k = k;
+    P.s_row = s_row;
+    P.s_k = s_k;
+    P.res = res_mc;
+    P.res_ld = res_ld;
+    P.res_plane = res_plane;
+    P.exps = exps_mc;
+    P.bits = bits;
+    P.n_mod = n_mod;
+    P.colmax = colmax_scratch;
+    P.done = reinterpret_cast<unsigned long long*>(done_mc);
+    mod_consts(n_mod, &P.mc);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    FPEMU_CUDA(cudaMemsetAsync(colmax_scratch, 0, (size_t)rows * 8, st));
+    dim3 g1((unsigned)((rows + 255) / 256), (unsigned)((k + kColmaxK - 1) / kColmaxK));
+    split_colmax_kernel<<<g1, 256, 0, st>>>(P, reinterpret_cast<unsigned long long*>(colmax_scratch));
+    FPEMU_CUDA(cudaGetLastError());
+    dim3 g2((unsigned)((rows + kTileR - 1) / kTileR), (unsigned)((res_ld + kTileK - 1) / kTileK));
+    split_strided_kernel<true><<<g2, 256, 0, st>>>(P);
+    FPEMU_CUDA(cudaGetLastError());
+    return FPEMU_OK;
+}
+
+int fpemu_wait_counters(const uint64_t* const* counters, int n, uint64_t target, int where, void* stream) {
+    if (n < 0 || n > kMaxWaitCounters) return fail(FPEMU_ERR_INVALID, "wait_counters: n=%d outside [0, %d]", n, kMaxWaitCounters);
+    if (n == 0) return FPEMU_OK;
+    if (!counters) return fail(FPEMU_ERR_INVALID, "wait_counters: null list");
+    CounterList L;
+    memset(&L, 0, sizeof L);
+    for (int i = 0; i < n; ++i) {
+        if (!counters[i] || reinterpret_cast<uintptr_t>(counters[i]) % 8 != 0)
+            return fail(FPEMU_ERR_INVALID, "wait_counters: counter %d null or misaligned", i);
+        L.p[i] = reinterpret_cast<const unsigned long long*>(counters[i]);
+    }
+    L.n = n;
+    wait_counters_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(L, (unsigned long long)target,
+                                                                         (int64_t)wait_budget_ns(), where);
+    FPEMU_CUDA(cudaGetLastError());
+    return FPEMU_OK;
+}
+
+int fpemu_signal_counter(uint64_t* counter, int multicast, void* stream) {
+    if (!counter || reinterpret_cast<uintptr_t>(counter) % 8 != 0)
+        return fail(FPEMU_ERR_INVALID, "signal_counter: null or misaligned counter");
+    signal_counter_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<unsigned long long*>(counter), multicast ? 1 : 0);
+    FPEMU_CUDA(cudaGetLastError());
+    return FPEMU_OK;
 }
 
 int fpemu_gemm_residues(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_res, const int8_t* b_res,

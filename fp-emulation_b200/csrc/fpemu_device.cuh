@@ -31,6 +31,7 @@ enum : int {
     kWaitDrainTma = 5,   // producer draining its loads at exit
     kWaitDrainMma = 6,   // MMA warp draining its MMAs at exit
     kWaitPass = 7,       // producer waiting for every CTA to finish issuing a modulus pass
+    kWaitCounter = 8,    // a stream-ordered wait on another GPU's progress counter
 };
 
 // The first device-side failure on this device (one copy per device that loads

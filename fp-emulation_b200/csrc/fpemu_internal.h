@@ -41,6 +41,7 @@ struct SplitParams {
     int64_t res_ld, res_plane;
     int32_t* exps;
     const uint64_t* colmax;  // strided variant only
+    unsigned long long* done;  // multicast variant only: per-CTA completion counter
     int bits, n_mod;
     ModConsts mc;
 };

@@ -43,6 +43,10 @@ SIGNATURES = {
                               _int, _vp, _sz, _vp]),
     "fpemu_gemm_workspace_size": (_sz, [_i64, _i64, _int]),
     "fpemu_gemm_crt_noalloc": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _vp, _vp, _int, _vp, _i64, _vp]),
+    "fpemu_split_mc": (_int, [_i64, _i64, _vp, _i64, _i64, _int, _int, _vp, _i64, _i64, _vp, _vp, _vp, _vp]),
+    "fpemu_split_mc_signals": (_i64, [_i64, _i64]),
+    "fpemu_wait_counters": (_int, [_vp, _int, ctypes.c_uint64, _int, _vp]),
+    "fpemu_signal_counter": (_int, [_vp, _int, _vp]),
     "fpemu_device_error": (_int, [_IP, _IP, _IP, _IP, _int]),
 }
 

@@ -1,0 +1,244 @@
+"""SM-free broadcast of B's residue chunks over NVLink, moved by the GPUs' copy
+engines through CUDA IPC.
+
+Why: NCCL's broadcast runs as kernels (about 24 GB/s per channel, one CTA per
+channel), so at the 8-GPU point it needs ~27 SMs for the whole 10 ms it takes
+to move B's 6.7 GB of residues -- SMs the persistent GEMM is using.  Copy
+engines need no SMs, so the transfer hides under the tensor work.
+
+Every rank owns one device buffer (cudaMalloc) holding B's residue chunks
+(chunk c = int8 [n_mod][W][ld] followed by its W column exponents) and shares it
+through CUDA IPC together with interprocess events.  Copies are pulls: the
+receiving rank's stream copies from the peer's buffer into its own after waiting
+on the peer's event.  A stream may only wait on an event after the peer has
+enqueued the matching record, so ranks publish "phase enqueued" keys through the
+process group's store and wait for the keys they depend on before enqueuing
+waits.  All data movement and all GPU-side ordering is stream/event based; the
+host only orders the enqueues.
+
+The topology is a pipelined chain root -> next -> ... -> last, each chunk in
+pieces: every GPU receives each byte once from one predecessor and sends it
+once to one successor, which keeps every copy engine on one NVLink flow.  (A
+scatter from the root followed by an all-gather, tried as well, ran at about
+half the chain's bandwidth: a GPU pulling from six peers at once.)  The chain
+is World-1 hops deep, so its fill latency grows with the rank count.
+"""
+from __future__ import annotations
+
+import atexit
+import os
+
+import torch
+import torch.distributed as dist
+from cuda.bindings import runtime as rt
+
+
+def _check(res, what):
+    err = res[0] if isinstance(res, tuple) else res
+    if err != rt.cudaError_t.cudaSuccess:
+        raise RuntimeError(f"{what} failed: {err}")
+    return res[1] if isinstance(res, tuple) and len(res) == 2 else res
+
+
+def _align256(x):
+    return (x + 255) // 256 * 256
+
+
+class _Ext:
+    """A device allocation exposed to torch through __cuda_array_interface__."""
+
+    def __init__(self, ptr, nbytes):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|i1", "data": (ptr, False),
+                                         "version": 3}
+
+
+class _IpcChunks:
+    """The shared part: a chunked device buffer, named per-chunk interprocess
+    events, handle exchange over the group, peers' buffers and events opened on
+    demand, and the store keys that order the ranks' enqueues.
+
+    Construction is collective over the group, so every rank builds its
+    transports in the same order; the construction serial within the group (with
+    the group's global ranks) names the store keys identically on every rank."""
+
+    _serials: dict = {}
+    EVENTS: tuple = ()
+
+    def __init__(self, group, root, device, chunk_bytes, n_chunks):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.root = root
+        self.device = device
+        self.n_chunks = n_chunks
+        self.chunk_bytes = chunk_bytes
+        self.store = dist.distributed_c10d._get_default_store()
+        self.calls = 0
+        members = tuple(dist.get_process_group_ranks(group)) if group is not None else ("world",)
+        serial = _IpcChunks._serials.get(members, 0)
+        _IpcChunks._serials[members] = serial + 1
+        self.key_prefix = f"fpemu_ce/{'-'.join(map(str, members))}/{serial}"
+        flags = rt.cudaEventDisableTiming | rt.cudaEventInterprocess
+        with torch.cuda.device(device):
+            self.nbytes = chunk_bytes * n_chunks
+            self.ptr = _check(rt.cudaMalloc(self.nbytes), "cudaMalloc")
+            self.buf = torch.as_tensor(_Ext(int(self.ptr), self.nbytes), device=device)
+            self.ev = {name: [_check(rt.cudaEventCreateWithFlags(flags), "cudaEventCreate")
+                              for _ in range(self._events_per_chunk(name) * n_chunks)]
+                       for name in self.EVENTS}
+            self.gemm_done = [torch.cuda.Event() for _ in range(n_chunks)]
+            mem_h = bytes(_check(rt.cudaIpcGetMemHandle(self.ptr), "cudaIpcGetMemHandle").reserved)
+            ev_h = {name: [bytes(_check(rt.cudaIpcGetEventHandle(e), "cudaIpcGetEventHandle").reserved)
+                           for e in evs] for name, evs in self.ev.items()}
+        self._table = [None] * self.world
+        dist.all_gather_object(self._table, (mem_h, ev_h), group=group)
+        self._peer_ptr = {}
+        self._peer_ev = {}
+        atexit.register(self.close)
+
+    def _events_per_chunk(self, name):
+        return 1
+
+    def peer_ptr(self, r):
+        if r not in self._peer_ptr:
+            h = rt.cudaIpcMemHandle_t()
+            h.reserved = self._table[r][0]
+            with torch.cuda.device(self.device):
+                self._peer_ptr[r] = int(_check(rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess),
+                                               "cudaIpcOpenMemHandle"))
+        return self._peer_ptr[r]
+
+    def peer_events(self, r, name):
+        if (r, name) not in self._peer_ev:
+            evs = []
+            with torch.cuda.device(self.device):
+                for hb in self._table[r][1][name]:
+                    eh = rt.cudaIpcEventHandle_t()
+                    eh.reserved = hb
+                    evs.append(_check(rt.cudaIpcOpenEventHandle(eh), "cudaIpcOpenEventHandle"))
+            self._peer_ev[(r, name)] = evs
+        return self._peer_ev[(r, name)]
+
+    def chunk_view(self, c):
+        return self.buf[c * self.chunk_bytes:(c + 1) * self.chunk_bytes]
+
+    def _key(self, rank, call, phase):
+        return f"{self.key_prefix}/{call}/{phase}/{rank}"
+
+    def _wait_keys(self, ranks, call, phase):
+        keys = [self._key(r, call, phase) for r in ranks]
+        if keys:
+            self.store.wait(keys)
+
+    def _publish(self, phase):
+        self.store.set(self._key(self.rank, self.calls, phase), "1")
+
+    def _forget(self, call, phases):
+        """Delete this rank's keys of an old call once no rank can still wait on them."""
+        if call >= 0:
+            for ph in phases:
+                self.store.delete_key(self._key(self.rank, call, ph))
+
+    @staticmethod
+    def _wait(stream, event, what="wait"):
+        _check(rt.cudaStreamWaitEvent(stream.cuda_stream, event, 0), what)
+
+    @staticmethod
+    def _record(stream, event):
+        _check(rt.cudaEventRecord(event, stream.cuda_stream), "record")
+
+    @staticmethod
+    def _copy(stream, dst, src, nbytes):
+        _check(rt.cudaMemcpyAsync(dst, src, nbytes, rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice,
+                                  stream.cuda_stream), "memcpy")
+
+    def after_gemm(self, c, stream):
+        """This rank's GEMM on chunk c is enqueued on `stream`: the chunk may be
+        overwritten by the next call once it has run."""
+        self.gemm_done[c].record(stream)
+
+    def close(self):
+        for ptr in self._peer_ptr.values():
+            try:
+                rt.cudaIpcCloseMemHandle(ptr)
+            except Exception:
+                pass
+        self._peer_ptr = {}
+
+
+class CeChain(_IpcChunks):
+    """Pipelined chain root -> next -> ... -> last; each chunk moves in `pieces`
+    pieces, rank r copying piece (c, q) from its predecessor as soon as the
+    predecessor's ``done[c][q]`` fires.  Phase "A" = all of this call's records
+    enqueued; a rank waits for its predecessor's "A" of this call before
+    enqueuing waits on it, and for its successor's "A" of the previous call
+    before overwriting what the successor read."""
+
+    EVENTS = ("done",)
+
+    def __init__(self, group, root, device, chunk_bytes, n_chunks, pieces=None):
+        self.pieces = int(os.environ.get("FPEMU_CE_PIECES", "8")) if pieces is None else pieces
+        super().__init__(group, root, device, chunk_bytes, n_chunks)
+        order = [(root + i) % self.world for i in range(self.world)]
+        pos = order.index(self.rank)
+        self.pred = order[pos - 1] if pos > 0 else None
+        self.succ = order[pos + 1] if pos + 1 < self.world else None
+        self.split_stream = torch.cuda.current_stream(device)
+        self.copy_stream = torch.cuda.Stream(device)
+
+    def _events_per_chunk(self, name):
+        return self.pieces
+
+    def _done(self, r, c, q):
+        evs = self.ev["done"] if r == self.rank else self.peer_events(r, "done")
+        return evs[c * self.pieces + q]
+
+    def _piece(self, q):
+        step = _align256(-(-self.chunk_bytes // self.pieces))
+        lo = min(q * step, self.chunk_bytes)
+        return lo, min(self.chunk_bytes, lo + step)
+
+    def root_begin(self, main_stream):
+        if self.calls > 0 and self.succ is not None:
+            self._wait_keys([self.succ], self.calls - 1, "A")
+        self.split_stream = main_stream
+
+    def root_before_write(self, c):
+        if self.calls > 0 and self.succ is not None:
+            for q in range(self.pieces):
+                self._wait(self.split_stream, self._done(self.succ, c, q))
+
+    def root_after_write(self, c):
+        for q in range(self.pieces):
+            self._record(self.split_stream, self._done(self.rank, c, q))
+
+    def root_end(self):
+        self._publish("A")
+        self.calls += 1
+
+    def pull(self):
+        i = self.calls
+        if i > 0 and self.succ is not None:
+            self._wait_keys([self.succ], i - 1, "A")
+        self._wait_keys([self.pred], i, "A")
+        cs = self.copy_stream
+        pred_ptr = self.peer_ptr(self.pred)
+        for c in range(self.n_chunks):
+            cs.wait_event(self.gemm_done[c])
+            base = c * self.chunk_bytes
+            for q in range(self.pieces):
+                lo, hi = self._piece(q)
+                self._wait(cs, self._done(self.pred, c, q), "wait pred")
+                if i > 0 and self.succ is not None:
+                    self._wait(cs, self._done(self.succ, c, q), "wait succ")
+                if hi > lo:
+                    self._copy(cs, int(self.ptr) + base + lo, pred_ptr + base + lo, hi - lo)
+                self._record(cs, self._done(self.rank, c, q))
+        self._publish("A")
+        self.calls += 1
+
+    def wait_chunk(self, c, stream):
+        self._wait(stream, self._done(self.rank, c, self.pieces - 1), "wait chunk")
+
+
+TRANSPORTS = {"ce": CeChain}

@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import warnings
 from dataclasses import dataclass
 
 import torch
@@ -38,9 +39,14 @@ COMM_SMS = int(os.environ.get("FPEMU_COMM_SMS", "16"))
 # element, the default) or "fp64" (B itself, 8 bytes per element; every rank then
 # splits the chunk locally -- less NVLink traffic for more split work per rank).
 BCAST_MODE = os.environ.get("FPEMU_BCAST", "residues")
-# How residues travel: "ce" (copy-engine chain over NVLink through CUDA IPC, no SMs;
-# see ce_chain.py) or "nccl" (NCCL broadcast kernels).
-TRANSPORT = os.environ.get("FPEMU_TRANSPORT", "ce")
+# How B's residues reach every rank:
+#  "nvls" (default): every rank splits a strip of each column chunk and stores the
+#         residues through an NVLink multicast address (nvls_transport.py); falls
+#         back to "ce" where the group has no multicast support;
+#  "ce":   the root splits B, copy engines relay the chunks along a chain of ranks
+#         through CUDA IPC (ce_transport.py);
+#  "nccl": the root splits B, NCCL broadcast kernels move the chunks.
+TRANSPORT = os.environ.get("FPEMU_TRANSPORT", "nvls")
 
 
 def shard_rows(m: int, world: int, rank: int):
@@ -158,20 +164,76 @@ def rowsharded_product(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, c
     return C
 
 
-_CHAINS = {}
+_TRANSPORTS = {}
 
 
 def _align256(x):
     return (x + 255) // 256 * 256
 
 
-def rowsharded_product_ce(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, chunk_cols=CHUNK_COLS):
-    """Same product, B's residues moved by the copy-engine chain (ce_chain.py): the
-    root splits each column chunk straight into its shared buffer, every other rank
-    pulls the chunk piece by piece from its predecessor, and each rank's GEMM on
-    chunk c starts when chunk c has landed -- no SMs spent on the transfer."""
-    from fp_emulation.ce_chain import CeChain
+def rowsharded_product_nvls(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, chunk_cols=CHUNK_COLS):
+    """Same product through the NVLS transport (nvls_transport.py)."""
+    from fp_emulation.nvls_transport import NvlsTransport
 
+    dev = A_local.device
+    plan = plan_column_chunks(n, chunk_cols)
+    key = ("nvls", id(group), root, dev.index, k, n, n_mod, tuple(plan))
+    tr = _TRANSPORTS.get(key)
+    if tr is None:
+        try:
+            tr = NvlsTransport(group, root, dev, k, n, n_mod, _res_ld(k), plan)
+        except RuntimeError as exc:  # no multicast mapping for this group or size
+            raise _NvlsSetupError(str(exc)) from exc
+        _TRANSPORTS[key] = tr
+    return tr.product(A_local, B, ops, bits)
+
+
+class _NvlsSetupError(RuntimeError):
+    pass
+
+
+_NVLS_OK = {}
+
+
+def rowsharded_product_auto(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, transport=None):
+    """The product through the configured transport ("nvls" -> "ce" when the
+    group has no NVLink multicast)."""
+    kind = transport or TRANSPORT
+    if BCAST_MODE != "residues" or kind == "nccl":
+        return rowsharded_product(A_local, B, n, k, bits, n_mod, ops, root, group)
+    if kind == "nvls":
+        gkey = id(group)
+        if gkey not in _NVLS_OK:
+            import torch.distributed._symmetric_memory  # noqa: F401  (multicast needs it)
+            from cuda.bindings import driver as drv
+
+            ok = drv.cuDeviceGetAttribute(drv.CUdevice_attribute.CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED,
+                                          A_local.device.index)[1] == 1
+            flags = [None] * dist.get_world_size(group)
+            dist.all_gather_object(flags, ok, group=group)
+            _NVLS_OK[gkey] = all(flags)
+        if _NVLS_OK[gkey]:
+            try:
+                return rowsharded_product_nvls(A_local, B, n, k, bits, n_mod, ops, root, group)
+            except _NvlsSetupError as exc:
+                warnings.warn(f"NVLS transport unavailable ({exc}); using the copy-engine chain")
+                _NVLS_OK[gkey] = False
+        kind = "ce"
+    return rowsharded_product_ce(A_local, B, n, k, bits, n_mod, ops, root, group, transport=kind)
+
+
+def rowsharded_product_ce(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, chunk_cols=CHUNK_COLS,
+                          transport=None):
+    """Same product, B's residues moved by the copy engines (ce_transport.py).
+
+    The root splits each column chunk straight into its shared buffer on a side
+    stream, so the splits run on the SMs the wave-balanced GEMM grid leaves free
+    while the root's GEMMs start on the first chunk; every other rank pulls the
+    chunks over NVLink and starts its GEMM on chunk c when chunk c has landed.
+    No SMs are spent on the transfer."""
+    from fp_emulation.ce_transport import TRANSPORTS
+
+    kind = transport or TRANSPORT
     rank = dist.get_rank(group)
     dev = A_local.device
     m = A_local.shape[0]
@@ -180,35 +242,39 @@ def rowsharded_product_ce(A_local, B, n, k, bits, n_mod, ops, root=0, group=None
     wmax = max(c1 - c0 for c0, c1 in plan)
     res_bytes = _align256(n_mod * wmax * ld)
     chunk_bytes = res_bytes + _align256(wmax * 4)
-    key = (id(group), root, dev.index, chunk_bytes, len(plan))
-    chain = _CHAINS.get(key)
-    if chain is None:
-        chain = _CHAINS[key] = CeChain(group, root, dev, chunk_bytes, len(plan))
+    key = (kind, id(group), root, dev.index, chunk_bytes, len(plan))
+    tr = _TRANSPORTS.get(key)
+    if tr is None:
+        tr = _TRANSPORTS[key] = TRANSPORTS[kind](group, root, dev, chunk_bytes, len(plan))
     stream = torch.cuda.current_stream(dev)
-    chain.begin()
     views = []
     for c, (c0, c1) in enumerate(plan):
         w = c1 - c0
-        blk = chain.chunk_view(c)
-        res = blk[: n_mod * w * ld].view(n_mod, w, ld)
-        exps = blk[res_bytes: res_bytes + 4 * w].view(torch.int32)
-        if rank == root:
-            chain.root_before_write(c, stream)
-            ops.split(B[:, c0:c1].T, bits, n_mod, res, exps)
-            chain.root_after_write(c, stream)
-        views.append((c0, c1, res, exps))
-    if rank != root:
-        chain.relay()
-    chain.publish()
+        blk = tr.chunk_view(c)
+        views.append((c0, c1, blk[: n_mod * w * ld].view(n_mod, w, ld),
+                      blk[res_bytes: res_bytes + 4 * w].view(torch.int32)))
+    if rank == root:
+        tr.root_begin(stream)
+        ss = tr.split_stream
+        if ss is not stream:
+            B.record_stream(ss)
+        with torch.cuda.stream(ss):
+            for c, (c0, c1, res, exps) in enumerate(views):
+                tr.root_before_write(c)
+                ops.split(B[:, c0:c1].T, bits, n_mod, res, exps)
+                tr.root_after_write(c)
+        tr.root_end()
+    else:
+        tr.pull()
     a_res = ops.empty_res(n_mod, m, ld)
     row_exp = ops.empty_exps(m)
     ops.split(A_local, bits, n_mod, a_res, row_exp)
     C = torch.empty((m, n), dtype=torch.float64, device=dev)
     for c, (c0, c1, res, exps) in enumerate(views):
-        chain.wait_chunk(c, stream)
+        tr.wait_chunk(c, stream)
         if m and c1 > c0:
             ops.gemm_crt(a_res, row_exp, res, exps, bits, C, c0, c1, k)
-        chain.after_gemm(c, stream)
+        tr.after_gemm(c, stream)
     return C
 
 
@@ -238,9 +304,12 @@ def ozaki2_int8_matmul_rowsharded(A_local, B, n: int | None = None, root: int = 
         raise RuntimeError("inner dimension k must be non-zero")
     n_mod = _n_moduli(k, bits)
     with torch.cuda.device(dev):
-        if BCAST_MODE == "residues" and TRANSPORT == "ce":
-            C = rowsharded_product_ce(A_local, B, n, k, bits, n_mod, _GpuOps(dev, comm_sms=0), root, group)
+        if dist.get_world_size(group) == 1:
+            from fp_emulation.ozaki import _ozaki2_forward
+
+            C = _ozaki2_forward(A_local, B, n_mod=n_mod)
         else:
-            C = rowsharded_product(A_local, B, n, k, bits, n_mod, _GpuOps(dev), root, group)
+            ops = _GpuOps(dev, comm_sms=None if TRANSPORT == "nccl" or BCAST_MODE != "residues" else 0)
+            C = rowsharded_product_auto(A_local, B, n, k, bits, n_mod, ops, root, group)
     _after_call("ozaki2_int8_matmul_rowsharded")
     return C if orig == torch.float64 else C.to(orig)

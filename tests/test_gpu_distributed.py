@@ -1,5 +1,5 @@
-"""The row-sharded multi-GPU product on real GPUs: 2 NCCL ranks as child
-processes (skipped with fewer than 2 GPUs).  Each rank computes its rows of C
+"""The row-sharded multi-GPU product on real GPUs: NCCL ranks as child
+processes (skipped with too few GPUs).  Each rank computes its rows of C
 through the pipelined broadcast of B's residues; the gathered result must be
 bit-identical to the oracle's full product."""
 from __future__ import annotations
@@ -50,37 +50,57 @@ def _worker(rank, world, port, m, k, n, q, transport="ce", calls=2):
         # Several calls in a row: buffers and events of the transport are reused.
         for _ in range(calls):
             C = ozaki2_int8_matmul_rowsharded(A_local, B_t, n=n, root=0)
+        # A second column count in the same group: a second transport channel,
+        # whose handshakes must not be confused with the first one's.
+        n2 = n // 2 + 1
+        C2 = ozaki2_int8_matmul_rowsharded(A_local, B_t[:, :n2].contiguous() if B_t is not None else None,
+                                           n=n2, root=0)
+        C = ozaki2_int8_matmul_rowsharded(A_local, B_t, n=n, root=0)
         torch.cuda.synchronize(dev)
         code = _lib.device_error(clear=True)
-        q.put((rank, "ok", (r0, r1, C.cpu().numpy(), code)))
+        q.put((rank, "ok", (r0, r1, C.cpu().numpy(), C2.cpu().numpy(), code)))
         torch.distributed.barrier(device_ids=[rank])
         torch.distributed.destroy_process_group()
     except Exception:
         q.put((rank, "error", traceback.format_exc()))
 
 
-@pytest.mark.parametrize("transport", ["ce", "nccl"])
-def test_rowsharded_two_gpus_bit_exact(transport):
+@pytest.mark.parametrize("world", [2, "all"])
+@pytest.mark.parametrize("transport", ["nvls", "ce", "nccl"])
+def test_rowsharded_multi_gpu_bit_exact(transport, world):
+    """world 2: root and last rank only; "all" (3 or more GPUs): the chain's middle
+    ranks both receive from a predecessor and feed a successor."""
     import torch
     import torch.multiprocessing as mp
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    have = torch.cuda.device_count()
+    if world == "all":
+        if have < 3:
+            pytest.skip("needs 3 or more GPUs")
+        world = have
+    elif have < world:
+        pytest.skip(f"needs {world} GPUs")
     m, k, n = 1000, 700, 1500
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, m, k, n, q, transport)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, m, k, n, q, transport)) for r in range(world)]
     for p in procs:
         p.start()
-    results = [q.get(timeout=300) for _ in range(2)]
+    results = [q.get(timeout=300) for _ in range(world)]
     for p in procs:
         p.join(timeout=60)
+    n2 = n // 2 + 1
     C = np.full((m, n), np.nan)
+    C2 = np.full((m, n2), np.nan)
     for rank, status, payload in results:
         assert status == "ok", payload
-        r0, r1, Cr, code = payload
+        r0, r1, Cr, C2r, code = payload
         assert code[0] == 0, code
         C[r0:r1] = Cr
+        C2[r0:r1] = C2r
     A, B = _problem(m, k, n)
-    np.testing.assert_array_equal(C.view(np.int64), oo.ozaki2_matmul(A, B).view(np.int64))
+    want = oo.ozaki2_matmul(A, B)
+    np.testing.assert_array_equal(C.view(np.int64), want.view(np.int64))
+    # Column exponents are per column, so the product with B[:, :n2] is C[:, :n2].
+    np.testing.assert_array_equal(C2.view(np.int64), want[:, :n2].view(np.int64))
