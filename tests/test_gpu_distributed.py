@@ -5,7 +5,6 @@ bit-identical to the oracle's full product."""
 from __future__ import annotations
 
 import os
-import socket
 import traceback
 from datetime import timedelta
 
@@ -17,12 +16,6 @@ from oracle import ozaki_oracle as oo
 pytestmark = pytest.mark.gpu
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
 def _problem(m, k, n):
     rng = np.random.default_rng(77)
     A = (rng.random((m, k)) - 0.5) * np.exp(1.5 * rng.standard_normal((m, k)))
@@ -30,16 +23,16 @@ def _problem(m, k, n):
     return A, B
 
 
-def _worker(rank, world, port, m, k, n, q, transport="ce", calls=2):
+def _worker(rank, world, store_file, m, k, n, q, transport="ce", calls=2):
     try:
         import torch
 
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
-                          FPEMU_CHUNK_COLS="512", FPEMU_TRANSPORT=transport)
+        os.environ.update(NCCL_NVLS_ENABLE="0", FPEMU_CHUNK_COLS="512", FPEMU_TRANSPORT=transport)
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
-        torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
-                                             timeout=timedelta(seconds=60))
+        # A file store: no TCP port to collide with an earlier test's sockets.
+        torch.distributed.init_process_group("nccl", init_method=f"file://{store_file}", rank=rank,
+                                             world_size=world, device_id=dev, timeout=timedelta(seconds=60))
         from fp_emulation import _lib
         from fp_emulation.distributed import ozaki2_int8_matmul_rowsharded, shard_rows
 
@@ -67,7 +60,7 @@ def _worker(rank, world, port, m, k, n, q, transport="ce", calls=2):
 
 @pytest.mark.parametrize("world", [2, "all"])
 @pytest.mark.parametrize("transport", ["nvls", "ce", "nccl"])
-def test_rowsharded_multi_gpu_bit_exact(transport, world):
+def test_rowsharded_multi_gpu_bit_exact(transport, world, tmp_path):
     """world 2: root and last rank only; "all" (3 or more GPUs): the chain's middle
     ranks both receive from a predecessor and feed a successor."""
     import torch
@@ -83,8 +76,8 @@ def test_rowsharded_multi_gpu_bit_exact(transport, world):
     m, k, n = 1000, 700, 1500
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, m, k, n, q, transport)) for r in range(world)]
+    store_file = str(tmp_path / "store")
+    procs = [ctx.Process(target=_worker, args=(r, world, store_file, m, k, n, q, transport)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in range(world)]
