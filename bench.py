@@ -48,7 +48,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--n", type=int, default=16384)
+    ap.add_argument("--config", type=int, choices=[2, 3], default=2,
+                    help="2: square n x n (the metric's workload); 3: m=131072, k=n=8192 with 1%% of A's rows x 2^40")
+    ap.add_argument("--n", type=int, default=16384, help="config 2 size")
     ap.add_argument("--phi", type=float, default=1.0)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-extras", action="store_true", help="skip DGEMM/cuBLASLt/CPU side numbers")
@@ -56,14 +58,28 @@ def parse_args():
     return ap.parse_args()
 
 
-def workload_config(n, phi, n_mod, world):
+def problem_shape(args):
+    """(M, N, K) of the workload: config 2 is n x n x n, config 3 is 131072 x 8192 x 8192."""
+    if args.config == 3:
+        return 131072, 8192, 8192
+    return args.n, args.n, args.n
+
+
+def workload_config(args, n_mod, world, transport=None):
+    M, N, K = problem_shape(args)
+    if args.config == 3:
+        desc = ("BASELINE config 3: m=131072, k=n=8192 FP64 GEMM, N(0,1) entries with 1% of A's rows "
+                "(seeded choice) scaled by 2^40")
+    else:
+        desc = f"BASELINE config 2 point n={N}: square FP64 GEMM, entries (U(0,1)-0.5)*exp({args.phi}*N(0,1))"
     return {
-        "workload": f"BASELINE config 2 point n={n}: square FP64 GEMM, entries (U(0,1)-0.5)*exp({phi}*N(0,1))",
-        "m": n, "n": n, "k": n, "n_mod": n_mod, "phi": phi,
-        "l2": "inputs larger than L2 (2 GiB per operand); no flush",
+        "workload": desc,
+        "m": M, "n": N, "k": K, "n_mod": n_mod, **({"phi": args.phi} if args.config == 2 else {}),
+        "l2": f"inputs larger than L2 ({8 * M * K / 2**30:.1f} and {8 * K * N / 2**30:.1f} GiB operands); no flush",
         "parallelism": "single GPU" if world == 1 else (
-            f"A row-sharded over {world} GPUs, B residues broadcast over NVLink "
-            f"({os.environ.get('FPEMU_TRANSPORT', 'nvls')} transport, {os.environ.get('FPEMU_BCAST', 'residues')})"),
+            f"A row-sharded over {world} GPUs, B residues to every GPU over NVLink "
+            f"({transport or os.environ.get('FPEMU_TRANSPORT', 'nvls')} transport, "
+            f"{os.environ.get('FPEMU_BCAST', 'residues')})"),
     }
 
 
@@ -163,6 +179,18 @@ def synth(torch, rows, cols, phi, seed, device):
     return (u - 0.5) * torch.exp(phi * e)
 
 
+def synth_config3_rows(torch, M, r0, r1, K, seed, device):
+    """Rows [r0, r1) of config 3's A: N(0,1), with 1 % of all M rows (a seeded
+    choice, the same on every rank) scaled by 2^40."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    A = torch.randn(r1 - r0, K, dtype=torch.float64, generator=g, device=device)
+    scaled = torch.randperm(M, generator=torch.Generator().manual_seed(seed + 7))[: M // 100]
+    local = scaled[(scaled >= r0) & (scaled < r1)] - r0
+    if local.numel():
+        A[local.to(device)] *= 2.0 ** 40
+    return A
+
+
 # ---------------------------------------------------------------- ours -----
 
 def run_ours(args):
@@ -182,16 +210,21 @@ def run_ours(args):
 
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     lib = _lib.load()
-    n, k = args.n, args.n
-    r0, r1 = shard_rows(n, world, rank)
+    M, n, k = problem_shape(args)
+    r0, r1 = shard_rows(M, world, rank)
     m = r1 - r0
     bits = 53
     n_mod = _n_moduli(k, bits)
     ld = _res_ld(k)
     root = 0
 
-    A = synth(torch, m, k, args.phi, args.seed + 1 + rank, dev)
-    B = synth(torch, k, n, args.phi, args.seed + 1000, dev) if rank == root else None
+    if args.config == 3:
+        A = synth_config3_rows(torch, M, r0, r1, k, args.seed + 1 + rank, dev)
+        B = torch.randn(k, n, dtype=torch.float64, device=dev,
+                        generator=torch.Generator(device=dev).manual_seed(args.seed + 1000)) if rank == root else None
+    else:
+        A = synth(torch, m, k, args.phi, args.seed + 1 + rank, dev)
+        B = synth(torch, k, n, args.phi, args.seed + 1000, dev) if rank == root else None
 
     a_res = torch.empty((n_mod, m, ld), dtype=torch.int8, device=dev)
     b_res = torch.empty((n_mod, n, ld), dtype=torch.int8, device=dev) if (world == 1 or rank == root) else None
@@ -289,7 +322,12 @@ def run_ours(args):
     if code[0]:
         raise RuntimeError(f"device-side failure in the timed region: {code}")
     ms_step = elapsed_ms / args.steps
-    flops = 2.0 * n * n * k
+    transport_used = None
+    if world > 1:
+        transport_used = fdist.TRANSPORT if fdist.BCAST_MODE == "residues" else "nccl"
+        if transport_used == "nvls" and not fdist._NVLS_OK.get(id(None), False):
+            transport_used = "ce"
+    flops = 2.0 * M * n * k
     value = flops / (ms_step * 1e-3) / 1e12
 
     if world == 1:
@@ -319,8 +357,19 @@ def run_ours(args):
         peak_burst = 2.0 * 1590.0
     # Our kernels per step: split A (1), split B on the root (column max + split: 2 per
     # chunk), one GEMM per chunk (1 chunk on a single GPU).
-    nch = 1 if world == 1 else n_chunks
-    launches = int(sum_over_ranks((1 + (2 * nch if rank == root else 0) + nch) * args.steps))
+    # Our kernels per step and rank.  One GPU: split A, split B (column max +
+    # split), the fused GEMM.  Root-split transports (ce, nccl): split A, split B
+    # per chunk on the root (2 kernels), one GEMM per chunk.  NVLS: split A, and
+    # per chunk two counter waits + the strip's 2 split kernels on the split
+    # stream, a wait + the GEMM + a signal on the GEMM stream, and on the root a
+    # wait + a signal beside its staging copies.
+    if world == 1:
+        per_rank = 4
+    elif transport_used == "nvls":
+        per_rank = 1 + 7 * n_chunks + (2 * n_chunks if rank == root else 0)
+    else:
+        per_rank = 1 + n_chunks + (2 * n_chunks if rank == root else 0)
+    launches = int(sum_over_ranks(per_rank * args.steps))
 
     # ---- end to end through the public op, host buffers ------------------
     e2e = None
@@ -411,14 +460,14 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int8", "emulated": "f64", "data": "synthetic (seeded, generated on device)",
-            "config": workload_config(n, args.phi, n_mod, world),
+            "config": workload_config(args, n_mod, world, transport_used),
             "e2e": e2e,
             "roofline": {"bound": "tensor", "kernel": "ozaki_gemm_kernel (fused INT8 GEMM + mod + CRT)",
                          "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
                          "peak_burst": round(peak_burst, 1), "frac_burst": round(achieved / peak_burst, 4),
                          "ops_per_launch": int8_ops, "launch_ms": round(gemm_ms, 3),
-                         "traffic": gemm_traffic_per_launch(n)},
+                         "traffic": gemm_traffic_per_launch(n) if args.config == 2 else None},
             "int8_tc_util": round(achieved / peak_burst, 4),
             "stages_ms": stages,
             "gpu_launches": launches,
@@ -479,14 +528,14 @@ def cpu_baseline(args, torch, r=256, c=256):
 
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    n = args.n
-    A, B = synthetic_block(n, 32, 32, args.phi, args.seed)
-    block_time(A, B, n, n)  # warm-up (also loads the compiled CRT)
-    A, B = synthetic_block(n, r, c, args.phi, args.seed)
-    est, blk, st = block_time(A, B, n, n)
-    return {"value": round(2.0 * n ** 3 / est / 1e12, 9), "unit": "TFLOPS", "cores": cores,
+    M, N, K = problem_shape(args)
+    A, B = synthetic_block(K, 32, 32, args.phi, args.seed)
+    block_time(A, B, M, N)  # warm-up (also loads the compiled CRT)
+    A, B = synthetic_block(K, r, c, args.phi, args.seed)
+    est, blk, st = block_time(A, B, M, N)
+    return {"value": round(2.0 * M * N * K / est / 1e12, 9), "unit": "TFLOPS", "cores": cores,
             "kind": crt_kind(),
-            "sample": f"{r}x{c} block of the n={n} product (full K), {blk:.1f} s wall; stages "
+            "sample": f"{r}x{c} block of the {M}x{N}x{K} product (full K), {blk:.1f} s wall; stages "
                       f"split_a/split_b/int32-matmul/crt = {', '.join(f'{x:.2f}' for x in st)} s, "
                       f"extrapolated to the full product ({est / 3600:.2f} h): reference torch op "
                       f"sequence + crt_reconstruct.cpp compiled from the reference source"}
@@ -505,27 +554,29 @@ def run_reference(args):
 
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    n = args.n
-    n_mod = n_moduli(n, 53)
+    M, N, K = problem_shape(args)
+    n_mod = n_moduli(K, 53)
     r, c = 128, 256
-    A, B = synthetic_block(n, r, c, args.phi, args.seed)
+    # The CPU path's time depends on the shapes, not the values: the block has
+    # the workload's K, config 2's value distribution.
+    A, B = synthetic_block(K, r, c, args.phi, args.seed)
     for _ in range(args.warmup):
-        block_time(A[:16], B[:, :16], n, n)
+        block_time(A[:16], B[:, :16], M, N)
     ests, walls = [], []
     for _ in range(args.steps):
-        est, blk, _ = block_time(A, B, n, n)
+        est, blk, _ = block_time(A, B, M, N)
         ests.append(est)
         walls.append(blk)
     est = statistics.mean(ests)
-    value = 2.0 * n ** 3 / est / 1e12
+    value = 2.0 * M * N * K / est / 1e12
     out = {
         "metric": METRIC, "value": round(value, 9), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(est * 1e3, 1), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int32", "emulated": "f64",
         "data": "synthetic (seeded)", "impl": "reference",
-        "config": workload_config(n, args.phi, n_mod, world),
+        "config": workload_config(args, n_mod, world),
         "cpu_baseline": {"value": round(value, 9), "unit": "TFLOPS", "cores": cores, "kind": crt_kind(),
-                         "sample": f"per step one {r}x{c} block of the n={n} product (full K, "
+                         "sample": f"per step one {r}x{c} block of the {M}x{N}x{K} product (full K, "
                                    f"{statistics.mean(walls):.1f} s wall) through the reference's CPU op "
                                    f"sequence + its crt_reconstruct.cpp, extrapolated to the full product"},
         "e2e": {"value": round(value, 9), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
