@@ -689,6 +689,18 @@ int fpemu_crt_reconstruct(int64_t m, int64_t n, int n_mod, const uint8_t* res, c
 int fpemu_gemm_crt(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_res, const int8_t* b_res,
                    int64_t res_ld, int64_t b_res_plane, const int32_t* row_exp, const int32_t* col_exp, int bits,
                    double* C, int64_t ldc, int max_ctas, void* workspace, size_t workspace_bytes, void* stream) {
+    return fpemu_gemm_crt_ex(m, n, k, n_mod, a_res, b_res, res_ld, b_res_plane, row_exp, col_exp, bits, C, ldc,
+                             FPEMU_C_F64, nullptr, max_ctas, workspace, workspace_bytes, stream);
+}
+
+int fpemu_gemm_crt_ex(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_res, const int8_t* b_res,
+                      int64_t res_ld, int64_t b_res_plane, const int32_t* row_exp, const int32_t* col_exp, int bits,
+                      void* C, int64_t ldc, int c_dtype, const void* bias, int max_ctas, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+    if (c_dtype != FPEMU_C_F64 && c_dtype != FPEMU_C_F32)
+        return fail(FPEMU_ERR_INVALID, "c_dtype=%d: expected FPEMU_C_F64 (0) or FPEMU_C_F32 (1)", c_dtype);
+    if (bias != nullptr && reinterpret_cast<uintptr_t>(bias) % (c_dtype == FPEMU_C_F32 ? 4 : 8) != 0)
+        return fail(FPEMU_ERR_INVALID, "bias is not aligned to its element size");
     DevInfo d;
     FPEMU_TRY(device_info(&d));
     FPEMU_TRY(bits_ok(bits));
@@ -706,8 +718,10 @@ int fpemu_gemm_crt(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_r
     P.n = (int)n;
     P.k = (int)k;
     P.n_mod = n_mod;
-    P.C = C;
+    P.C = static_cast<double*>(C);
     P.ldc = ldc;
+    P.bias = bias;
+    P.c_f32 = c_dtype == FPEMU_C_F32;
     P.row_exp = row_exp;
     P.col_exp = col_exp;
     P.two_bits = 2 * bits;
@@ -766,6 +780,14 @@ int fpemu_gemm_crt_noalloc(int64_t m, int64_t n, int64_t k, int n_mod, const int
 int fpemu_ozaki2_dgemm(int64_t m, int64_t n, int64_t k, const double* A, int64_t sA_row, int64_t sA_col,
                        const double* B, int64_t sB_row, int64_t sB_col, double* C, int64_t ldc, int bits,
                        int n_mod, void* workspace, size_t workspace_bytes, void* stream) {
+    return fpemu_ozaki2_gemm_ex(m, n, k, A, sA_row, sA_col, B, sB_row, sB_col, C, ldc, FPEMU_C_F64, nullptr, bits,
+                                n_mod, workspace, workspace_bytes, stream);
+}
+
+int fpemu_ozaki2_gemm_ex(int64_t m, int64_t n, int64_t k, const double* A, int64_t sA_row, int64_t sA_col,
+                         const double* B, int64_t sB_row, int64_t sB_col, void* C, int64_t ldc, int c_dtype,
+                         const void* bias, int bits, int n_mod, void* workspace, size_t workspace_bytes,
+                         void* stream) {
     DevInfo d;
     FPEMU_TRY(device_info(&d));
     FPEMU_TRY(bits_ok(bits));
@@ -791,8 +813,8 @@ int fpemu_ozaki2_dgemm(int64_t m, int64_t n, int64_t k, const double* A, int64_t
     uint64_t* colmax = reinterpret_cast<uint64_t*>(ws + L.colmax);
     FPEMU_TRY(fpemu_split(m, k, A, sA_row, sA_col, bits, n_mod, a_res, L.res_ld, m * L.res_ld, re, colmax, stream));
     FPEMU_TRY(fpemu_split(n, k, B, sB_col, sB_row, bits, n_mod, b_res, L.res_ld, n * L.res_ld, ce, colmax, stream));
-    return fpemu_gemm_crt(m, n, k, n_mod, a_res, b_res, L.res_ld, n * L.res_ld, re, ce, bits, C, ldc, 0,
-                          ws + L.scratch, L.total - L.scratch, stream);
+    return fpemu_gemm_crt_ex(m, n, k, n_mod, a_res, b_res, L.res_ld, n * L.res_ld, re, ce, bits, C, ldc, c_dtype,
+                             bias, 0, ws + L.scratch, L.total - L.scratch, stream);
 }
 
 int fpemu_device_error(int* code, int* where, int* block, int* detail, int clear) {

@@ -64,8 +64,10 @@ struct GemmParams {
     int tiles_m, tiles_n, num_tiles;
     int band_rows;         // tile rows per raster band
     void* out;             // raw int32 / uint8 residues, [n_mod][m][n] (modes 0, 1)
-    double* C;             // mode 2
+    double* C;             // mode 2 (float* when c_f32)
     int64_t ldc;
+    const void* bias;      // mode 2, optional: per-column bias in C's type, added after the cast
+    int c_f32;             // mode 2: C is float (the double result rounded to nearest)
     const int32_t* row_exp;
     const int32_t* col_exp;
     int two_bits;

@@ -80,6 +80,20 @@ __device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, ui
     return a | (b << 8) | (c << 16) | (d << 24);
 }
 
+// Write one reconstructed value: the double result, or its round-to-nearest
+// float when C is float32, then the optional per-column bias added in C's type
+// -- the order of the reference's `matmul(...).to(dtype)` followed by `+ bias`.
+__device__ __forceinline__ void store_c(const GemmParams& P, double* crow, int64_t row, int col, double v) {
+    if (P.c_f32) {
+        float f = __double2float_rn(v);
+        if (P.bias) f = __fadd_rn(f, static_cast<const float*>(P.bias)[col]);
+        reinterpret_cast<float*>(P.C)[row * P.ldc + col] = f;
+    } else {
+        if (P.bias) v = __dadd_rn(v, static_cast<const double*>(P.bias)[col]);
+        crow[col] = v;
+    }
+}
+
 // One kernel for both CTA-group sizes.  With CG = 2 the grid is made of
 // 2-CTA clusters; a pair owns a 256 x BN output tile: each CTA stages its 128
 // rows of A and its BN/2 rows of B, the leader (cluster rank 0) issues the
@@ -379,8 +393,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
                             const int col = cb + j;
-                            if (col < P.n)
-                                crow[col] = crt_scale(crt_finish(hi[j], lo[j], P.cc), re, P.col_exp[col], P.two_bits);
+                            if (col < P.n) {
+                                const double v = crt_scale(crt_finish(hi[j], lo[j], P.cc), re, P.col_exp[col],
+                                                           P.two_bits);
+                                store_c(P, crow, row, col, v);
+                            }
                         }
                     }
                 }

@@ -22,6 +22,8 @@ FPEMU_ERR_WORKSPACE = 4
 FPEMU_ERR_CUDA = 5
 FPEMU_ERR_TIMEOUT = 6
 FPEMU_ERR_NO_DEVICE = 7
+FPEMU_C_F64 = 0
+FPEMU_C_F32 = 1
 
 # Every symbol include/fpemu.h declares, with its ctypes signature.
 _i64, _int, _sz, _vp, _dp = ctypes.c_int64, ctypes.c_int, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_double
@@ -42,6 +44,10 @@ SIGNATURES = {
     "fpemu_gemm_crt": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _i64, _vp, _vp, _int, _vp, _i64,
                               _int, _vp, _sz, _vp]),
     "fpemu_gemm_workspace_size": (_sz, [_i64, _i64, _int]),
+    "fpemu_ozaki2_gemm_ex": (_int, [_i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _int, _vp,
+                                    _int, _int, _vp, _sz, _vp]),
+    "fpemu_gemm_crt_ex": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _i64, _vp, _vp, _int, _vp, _i64,
+                                 _int, _vp, _int, _vp, _sz, _vp]),
     "fpemu_gemm_crt_noalloc": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _vp, _vp, _int, _vp, _i64, _vp]),
     "fpemu_split_mc": (_int, [_i64, _i64, _vp, _i64, _i64, _int, _int, _vp, _i64, _i64, _vp, _vp, _vp, _vp]),
     "fpemu_split_mc_signals": (_i64, [_i64, _i64]),

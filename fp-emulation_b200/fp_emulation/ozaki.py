@@ -163,10 +163,29 @@ def _workspace(m, n, k, n_mod, dev):
     return torch.empty((nbytes,), dtype=torch.uint8, device=dev)
 
 
-def _ozaki2_forward(A, B, n_mod=None):
+def _fused_output(orig_dtype, bias, n, dev):
+    """(c_dtype, torch dtype of C, bias to pass) for the fused epilogue: float64
+    and float32 outputs are written by the kernel (the float32 one rounded from
+    the double result, as ``.to(torch.float32)`` does), with the bias added in
+    the output's type; other dtypes come back as float64 for torch to finish."""
+    if orig_dtype == torch.float32:
+        c_dtype, out_dtype = _lib.FPEMU_C_F32, torch.float32
+    else:
+        c_dtype, out_dtype = _lib.FPEMU_C_F64, torch.float64
+    fused_bias = None
+    if bias is not None and orig_dtype in (torch.float32, torch.float64):
+        if bias.shape != (n,):
+            raise RuntimeError(f"bias of shape {tuple(bias.shape)} does not match {n} output columns")
+        fused_bias = bias.to(device=dev, dtype=out_dtype).contiguous()
+    return c_dtype, out_dtype, fused_bias
+
+
+def _ozaki2_forward(A, B, n_mod=None, bias=None):
     """ozaki.py:95-119: scale -> modular INT8 matmuls -> CRT reconstruct, as one
     C call (split A, split B, fused GEMM + CRT) on the current stream.
-    ``n_mod`` overrides the reference's modulus count (for sweeps)."""
+    ``n_mod`` overrides the reference's modulus count (for sweeps).  ``bias``
+    (n values) is added after the cast to the input's dtype -- nn.py:20-21's
+    ``out + self.bias`` -- fused into the epilogue for float64/float32."""
     bits = _PRECISION_BITS.get(A.dtype)
     if bits is None:
         supported = ", ".join(str(d) for d in _PRECISION_BITS)
@@ -187,17 +206,50 @@ def _ozaki2_forward(A, B, n_mod=None):
                            "(the reference's amax over an empty dimension fails the same way)")
     if n_mod is None:
         n_mod = _n_moduli(k, bits)
-    C = torch.empty((m, n), dtype=torch.float64, device=dev)
+    c_dtype, out_dtype, fused_bias = _fused_output(orig_dtype, bias, n, dev)
+    C = torch.empty((m, n), dtype=out_dtype, device=dev)
     if m and n:
         with torch.cuda.device(dev):
             ws = _workspace(m, n, k, n_mod, dev)
-            st = _lib.load().fpemu_ozaki2_dgemm(
+            st = _lib.load().fpemu_ozaki2_gemm_ex(
                 m, n, k, A.data_ptr(), A.stride(0), A.stride(1), B.data_ptr(), B.stride(0), B.stride(1),
-                C.data_ptr(), n, bits, n_mod, ws.data_ptr(), ws.numel(), _stream(dev))
+                C.data_ptr(), n, c_dtype, None if fused_bias is None else fused_bias.data_ptr(), bits, n_mod,
+                ws.data_ptr(), ws.numel(), _stream(dev))
         _lib.check(st, "ozaki2_int8_matmul")
         _after_call("ozaki2_int8_matmul")
-    if orig_dtype != torch.float64:
+    elif fused_bias is not None:
+        C += fused_bias
+    if C.dtype != orig_dtype:
         C = C.to(orig_dtype)
+    if bias is not None and fused_bias is None:
+        C = C + bias
+    return C
+
+
+def _gemm_crt_cached(A, b_res, col_exp, n_mod, bias=None):
+    """C = A @ B from A (float64 [m, k], split here) and B's cached split
+    (b_res int8 [n_mod, n, ld], col_exp int32 [n]) -- the static-operand reuse
+    path; the result is what _ozaki2_forward(A, B, bias=bias) returns."""
+    dev = _require_cuda(A, b_res, col_exp)
+    bits = 53
+    m, k = A.shape
+    n = b_res.shape[1]
+    ld = b_res.shape[2]
+    c_dtype, out_dtype, fused_bias = _fused_output(torch.float64, bias, n, dev)
+    C = torch.empty((m, n), dtype=out_dtype, device=dev)
+    if m and n:
+        a_res, row_exp = _split(A, bits, n_mod)
+        lib = _lib.load()
+        with torch.cuda.device(dev):
+            ws = torch.empty((max(lib.fpemu_gemm_workspace_size(m, n, n_mod), 256),), dtype=torch.uint8, device=dev)
+            st = lib.fpemu_gemm_crt_ex(m, n, k, n_mod, a_res.data_ptr(), b_res.data_ptr(), ld, b_res.stride(0),
+                                       row_exp.data_ptr(), col_exp.data_ptr(), bits, C.data_ptr(), n, c_dtype,
+                                       None if fused_bias is None else fused_bias.data_ptr(), 0, ws.data_ptr(),
+                                       ws.numel(), _stream(dev))
+        _lib.check(st, "ozaki2_int8_matmul (cached operand)")
+        _after_call("ozaki2_int8_matmul")
+    elif fused_bias is not None:
+        C += fused_bias
     return C
 
 

@@ -82,6 +82,19 @@ int fpemu_ozaki2_dgemm(int64_t m, int64_t n, int64_t k, const double *A, int64_t
                        double *C, int64_t ldc, int bits, int n_mod, void *workspace,
                        size_t workspace_bytes, void *stream);
 
+/* Output element types of the _ex entry points. */
+#define FPEMU_C_F64 0
+#define FPEMU_C_F32 1
+
+/* fpemu_ozaki2_dgemm with the output's dtype cast and an nn.Linear bias fused
+ * into the epilogue: C (c_dtype) = cast(A @ B) + bias[j], in that order and
+ * with one rounding each -- ozaki.py:117-118 (`.to(orig_dtype)`) followed by
+ * nn.py:20-21 (`out + self.bias`).  bias: n elements of C's type, or NULL. */
+int fpemu_ozaki2_gemm_ex(int64_t m, int64_t n, int64_t k, const double *A, int64_t sA_row,
+                         int64_t sA_col, const double *B, int64_t sB_row, int64_t sB_col,
+                         void *C, int64_t ldc, int c_dtype, const void *bias, int bits, int n_mod,
+                         void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---- stages (each is also the parity tap for one step of the reference) -- */
 
 /* ozaki.py:32-46 (_scale_to_int + _residues) for one operand, fused:
@@ -123,6 +136,14 @@ int fpemu_gemm_crt(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t *a_r
                    const int32_t *row_exp, const int32_t *col_exp, int bits, double *C,
                    int64_t ldc, int max_ctas, void *workspace, size_t workspace_bytes,
                    void *stream);
+
+/* fpemu_gemm_crt with the output cast and bias of fpemu_ozaki2_gemm_ex (used
+ * with cached residues of a static operand, e.g. an nn.Linear weight). */
+int fpemu_gemm_crt_ex(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t *a_res,
+                      const int8_t *b_res, int64_t res_ld, int64_t b_res_plane,
+                      const int32_t *row_exp, const int32_t *col_exp, int bits, void *C,
+                      int64_t ldc, int c_dtype, const void *bias, int max_ctas, void *workspace,
+                      size_t workspace_bytes, void *stream);
 
 /* Allocation-free variant of fpemu_gemm_crt.  It has no counterpart in the
  * reference.  For callers that cannot allocate device memory -- code running
