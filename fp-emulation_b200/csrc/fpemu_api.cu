@@ -294,6 +294,12 @@ int band_rows() {
     return v < 1 ? 1 : (v > 1024 ? 1024 : v);
 }
 
+// Interleaved final passes of the modulus-major schedule (FPEMU_GEMM_TAIL=0 turns it off).
+int gemm_tail() {
+    const char* s = getenv("FPEMU_GEMM_TAIL");
+    return (s && atoi(s) == 0) ? 0 : 1;
+}
+
 // Schedule of the fused kernel: modulus-major unless FPEMU_GEMM_SCHED=tile.
 int gemm_sched() {
     const char* s = getenv("FPEMU_GEMM_SCHED");
@@ -728,6 +734,7 @@ int fpemu_gemm_crt_ex(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* 
     P.scratch = static_cast<uint8_t*>(workspace);
     P.scratch_slot = MainCfg::slot_bytes(n_mod);
     P.sched = sched;
+    P.tail = gemm_tail();
     if (sched == kSchedModulusMajor) {
         P.pass_ctr = reinterpret_cast<unsigned int*>(P.scratch + pass_ctr_offset(d, m, n, n_mod, sched));
         FPEMU_CUDA(cudaMemsetAsync(P.pass_ctr, 0, 256, static_cast<cudaStream_t>(stream)));

@@ -74,6 +74,7 @@ struct GemmParams {
     uint8_t* scratch;      // mode 2: residue staging
     int64_t scratch_slot;  // bytes of one staging slot (one CTA's share of one tile)
     int sched;             // GemmSched
+    int tail;              // modulus-major: interleave the last two passes (CRT next to light epilogues)
     unsigned int* pass_ctr;  // modulus-major: n_mod zeroed counters aligning the producers per pass
     uint64_t budget_ns;    // bound on every mbarrier wait
     ModConsts mc;

@@ -2,9 +2,13 @@
 // persistent, warp-specialised tcgen05 kernel (replaces the reference's
 // cuBLASLt strided-batched GEMM + mod_reduce + crt_kernel, crt_kernel.cu:6-146).
 //
-// Work: output tiles of 128 x BN; a CTA takes tiles round-robin and, for each
-// tile, runs the full K loop once per modulus l = 0 .. n_mod-1 (tile-major), so
-// all residues of a tile are produced by one CTA back to back.
+// Work: output tiles of kTileM x BN (256 x 256 for a CTA pair); a unit (CTA or
+// pair) owns tiles round-robin and runs the full K loop once per (tile,
+// modulus).  Default order, modulus-major: every unit sweeps its tiles for
+// modulus 0, then 1, ..., with the units aligned at each pass boundary so the
+// grid streams one residue plane at a time through L2; the last two passes
+// are interleaved (see unit_at).  Tile-major (all moduli of a tile back to
+// back) is the bounded-staging alternative.
 //
 // Roles (one CTA per SM):
 //   warp 0, one thread   TMA producer: A and B residue tiles [128 x 128 B] and
@@ -152,13 +156,28 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     // This CTA (pair) owns tiles r = unit, unit + num_units, ... (in band-raster
     // order) and walks (tile, modulus) units in the order P.sched selects.  All
     // three roles generate the same sequence.
+    //
+    // Modulus-major with an interleaved tail (P.tail): the last two passes a =
+    // n_mod-2 and b = n_mod-1 are merged as (0,a) (1,a) (0,b) (2,a) (1,b) ...
+    // (T-1,a) (T-2,b) (T-1,b), so each tile's CRT epilogue (b, about twice its
+    // MMA time in FP64 work) alternates with a light epilogue (a) instead of
+    // all CRTs queueing behind the last pass's MMAs.  (i,a) still precedes
+    // (i,b), whose CRT reads the plane staged at (i,a).
     const int my_tiles = (P.num_tiles - unit + num_units - 1) / num_units;
     const int my_units = my_tiles * P.n_mod;
+    const bool tail = P.sched != kSchedTileMajor && P.tail && P.n_mod >= 2;
+    const int tail_base = (P.n_mod - 2) * my_tiles;
     auto unit_at = [&](int idx, int& tile, int& l) {
         int i;
         if (P.sched == kSchedTileMajor) {
             i = idx / P.n_mod;
             l = idx - i * P.n_mod;
+        } else if (tail && idx >= tail_base) {
+            const int j = idx - tail_base;
+            if (j == 0) { i = 0; l = P.n_mod - 2; }
+            else if (j == 2 * my_tiles - 1) { i = my_tiles - 1; l = P.n_mod - 1; }
+            else if (j & 1) { i = (j + 1) >> 1; l = P.n_mod - 2; }
+            else { i = (j >> 1) - 1; l = P.n_mod - 1; }
         } else {
             l = idx / my_tiles;
             i = idx - l * my_tiles;
@@ -175,7 +194,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             for (int idx = 0; ok && idx < my_units; ++idx) {
                 int tile, l, tm, tn;
                 unit_at(idx, tile, l);
-                if (P.pass_ctr != nullptr && l > 0 && idx == l * my_tiles) {
+                // (With the interleaved tail, pass b has no barrier of its own: it
+                // runs inside the merged final phase that pass a's barrier opens.)
+                if (P.pass_ctr != nullptr && l > 0 && idx == l * my_tiles && !(tail && l == P.n_mod - 1)) {
                     // Modulus-major: start pass l only when every CTA has issued all of
                     // pass l-1, so the whole grid streams one modulus plane at a time and
                     // its A band stays in L2 (pairs with one tile fewer would otherwise
