@@ -78,7 +78,7 @@ def workload_config(args, n_mod, world, transport=None):
         "l2": f"inputs larger than L2 ({8 * M * K / 2**30:.1f} and {8 * K * N / 2**30:.1f} GiB operands); no flush",
         "parallelism": "single GPU" if world == 1 else (
             f"A row-sharded over {world} GPUs, B residues to every GPU over NVLink "
-            f"({transport or os.environ.get('FPEMU_TRANSPORT', 'nvls')} transport, "
+            f"({transport or os.environ.get('FPEMU_TRANSPORT', 'ce')} transport, "
             f"{os.environ.get('FPEMU_BCAST', 'residues')})"),
     }
 

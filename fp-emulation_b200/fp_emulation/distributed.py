@@ -40,13 +40,15 @@ COMM_SMS = int(os.environ.get("FPEMU_COMM_SMS", "16"))
 # splits the chunk locally -- less NVLink traffic for more split work per rank).
 BCAST_MODE = os.environ.get("FPEMU_BCAST", "residues")
 # How B's residues reach every rank:
-#  "nvls" (default): every rank splits a strip of each column chunk and stores the
-#         residues through an NVLink multicast address (nvls_transport.py); falls
-#         back to "ce" where the group has no multicast support;
-#  "ce":   the root splits B, copy engines relay the chunks along a chain of ranks
-#         through CUDA IPC (ce_transport.py);
+#  "ce" (default): the root splits B, copy engines relay the chunks along a chain
+#         of ranks through CUDA IPC (ce_transport.py);
+#  "nvls": every rank splits a strip of each column chunk and stores the residues
+#         through an NVLink multicast address (nvls_transport.py); falls back to
+#         "ce" where the group has no multicast support.  Opt-in: measured slower
+#         than "ce" at 8 GPUs (the multicast splits slow the concurrent GEMMs),
+#         and its counter waits timed out when a chunk's GEMM grid covered every SM;
 #  "nccl": the root splits B, NCCL broadcast kernels move the chunks.
-TRANSPORT = os.environ.get("FPEMU_TRANSPORT", "nvls")
+TRANSPORT = os.environ.get("FPEMU_TRANSPORT", "ce")
 
 
 def shard_rows(m: int, world: int, rank: int):
