@@ -294,10 +294,13 @@ int band_rows() {
     return v < 1 ? 1 : (v > 1024 ? 1024 : v);
 }
 
-// Interleaved final passes of the modulus-major schedule (FPEMU_GEMM_TAIL=0 turns it off).
+// Interleaved final passes of the modulus-major schedule (FPEMU_GEMM_TAIL=1).  Off by
+// default: measured on B200 it lowers the cycles of the last passes at n = 16384 but
+// raises power (the FP64 CRT runs beside the MMAs), so under the 1 kW cap the clock
+// drops and the product is 1 % slower; at m = 131072, k = n = 8192 it is 2.5 % slower.
 int gemm_tail() {
     const char* s = getenv("FPEMU_GEMM_TAIL");
-    return (s && atoi(s) == 0) ? 0 : 1;
+    return (s && atoi(s) == 1) ? 1 : 0;
 }
 
 // Schedule of the fused kernel: modulus-major unless FPEMU_GEMM_SCHED=tile.

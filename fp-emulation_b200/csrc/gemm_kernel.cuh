@@ -6,9 +6,9 @@
 // pair) owns tiles round-robin and runs the full K loop once per (tile,
 // modulus).  Default order, modulus-major: every unit sweeps its tiles for
 // modulus 0, then 1, ..., with the units aligned at each pass boundary so the
-// grid streams one residue plane at a time through L2; the last two passes
-// are interleaved (see unit_at).  Tile-major (all moduli of a tile back to
-// back) is the bounded-staging alternative.
+// grid streams one residue plane at a time through L2 (optionally with the
+// last two passes interleaved, see unit_at).  Tile-major (all moduli of a
+// tile back to back) is the bounded-staging alternative.
 //
 // Roles (one CTA per SM):
 //   warp 0, one thread   TMA producer: A and B residue tiles [128 x 128 B] and
@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     // order) and walks (tile, modulus) units in the order P.sched selects.  All
     // three roles generate the same sequence.
     //
-    // Modulus-major with an interleaved tail (P.tail): the last two passes a =
+    // Modulus-major, optionally with an interleaved tail (P.tail): the last two passes a =
     // n_mod-2 and b = n_mod-1 are merged as (0,a) (1,a) (0,b) (2,a) (1,b) ...
     // (T-1,a) (T-2,b) (T-1,b), so each tile's CRT epilogue (b, about twice its
     // MMA time in FP64 work) alternates with a light epilogue (a) instead of

@@ -269,13 +269,13 @@ def test_nonfinite_rows_give_nan(torch_cuda):
     np.testing.assert_array_equal(C[mask], want[mask])
 
 
-@pytest.mark.parametrize("sched", ["modulus", "modulus-plain", "tile"])
+@pytest.mark.parametrize("sched", ["modulus", "modulus-tail", "tile"])
 @pytest.mark.parametrize("ctas", ["1", "2"])
 @pytest.mark.parametrize("m,k,n", [(300, 520, 700), (513, 1100, 257), (1000, 300, 1000), (2600, 200, 700)])
 def test_gemm_configurations_agree(torch_cuda, monkeypatch, sched, ctas, m, k, n):
     """The CTA-pair GEMM (default) and the single-CTA GEMM (FPEMU_GEMM_CTAS=1),
-    each with the modulus-major schedule (default: last two passes
-    interleaved; "modulus-plain": FPEMU_GEMM_TAIL=0) and the tile-major one
+    each with the modulus-major schedule (default; "modulus-tail": the last
+    two passes interleaved, FPEMU_GEMM_TAIL=1) and the tile-major one
     (FPEMU_GEMM_SCHED=tile), must reproduce the oracle bit for bit, in the
     fused mode and in both parity taps."""
     torch = torch_cuda
@@ -284,7 +284,7 @@ def test_gemm_configurations_agree(torch_cuda, monkeypatch, sched, ctas, m, k, n
 
     monkeypatch.setenv("FPEMU_GEMM_CTAS", ctas)
     monkeypatch.setenv("FPEMU_GEMM_SCHED", "tile" if sched == "tile" else "modulus")
-    monkeypatch.setenv("FPEMU_GEMM_TAIL", "0" if sched == "modulus-plain" else "1")
+    monkeypatch.setenv("FPEMU_GEMM_TAIL", "1" if sched == "modulus-tail" else "0")
     A, B = _rand_case(m + k + n, m, k, n, kind="wide")
     C, st = oo.ozaki2_matmul(A, B, stages=True)
     got = ozaki2_int8_matmul(_cuda(torch, A), _cuda(torch, B)).cpu().numpy()
