@@ -1,0 +1,73 @@
+"""Index arithmetic of the multi-GPU transports, checked on the CPU: every
+byte range a kernel or a copy writes lies inside its own region of the
+shared buffer, regions do not overlap, and the strips and pieces partition
+their chunks exactly (no GPU needed)."""
+from __future__ import annotations
+
+import itertools
+
+import pytest
+
+from fp_emulation.distributed import plan_column_chunks
+from fp_emulation.nvls_transport import NvlsLayout, _even_split
+from fp_emulation.ozaki import _res_ld
+
+
+@pytest.mark.parametrize("w,parts", [(0, 3), (1, 8), (7, 8), (256, 8), (476, 8), (2048, 8), (2047, 3), (5, 2)])
+def test_even_split_partitions(w, parts):
+    spans = [_even_split(w, parts, i) for i in range(parts)]
+    assert spans[0][0] == 0 and spans[-1][1] == w
+    for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
+        assert a1 == b0 and a0 <= a1
+    sizes = [s1 - s0 for s0, s1 in spans]
+    assert max(sizes) - min(sizes) <= 1
+
+
+CASES = [(2, 700, 24, 1500, 512), (8, 700, 24, 1500, 512), (3, 129, 24, 751, 512), (8, 16384, 25, 16384, 2048),
+         (8, 8192, 25, 8192, 2048), (4, 16384, 25, 16384, 2048), (8, 64, 24, 3, 256), (5, 4097, 25, 2600, 1024)]
+
+
+@pytest.mark.parametrize("world,k,n_mod,n,chunk", CASES)
+def test_nvls_layout_writes_stay_in_their_regions(world, k, n_mod, n, chunk):
+    ld = _res_ld(k)
+    plan = plan_column_chunks(n, chunk)
+    L = NvlsLayout(world, k, n_mod, ld, plan)
+    assert L.pitch >= 2 and L.res_bytes % 256 == 0 and L.chunk_bytes % 256 == 0 and L.slot_bytes % 256 == 0
+    for j, (c0, c1) in enumerate(plan):
+        w = c1 - c0
+        assert sum(s1 - s0 for s0, s1 in L.strips[j]) == w
+        lo_chunk, hi_chunk = j * L.chunk_bytes, (j + 1) * L.chunk_bytes
+        res_spans = []
+        for q in range(world):
+            span = L.residue_span(j, q)
+            st = L.staging_span(j, q)
+            if span is None:
+                assert st is None
+                continue
+            (r0, r1), (e0, e1) = span
+            assert lo_chunk <= r0 <= r1 < lo_chunk + L.res_bytes          # residues in the chunk's residue part
+            assert lo_chunk + L.res_bytes <= e0 <= e1 < hi_chunk           # exponents after them
+            assert r0 % 16 == 0 and e0 % 4 == 0                           # multimem.st alignment
+            s0, s1 = L.strips[j][q]
+            # Each plane's rows of this strip: disjoint from the other strips' rows of that plane.
+            res_spans.append((s0, s1))
+            a0, a1 = st
+            slot0 = L.stage_off + j * L.slot_bytes
+            assert slot0 <= a0 <= a1 < slot0 + L.slot_bytes
+        for (a0, a1), (b0, b1) in itertools.combinations(res_spans, 2):
+            assert a1 <= b0 or b1 <= a0
+    for kind, j in itertools.product(range(3), range(len(plan))):
+        off = L.counter(kind, j)
+        assert L.cnt_off <= off and off + 8 <= L.total and off % 8 == 0
+    assert L.stage_off == len(plan) * L.chunk_bytes and L.cnt_off == L.stage_off + len(plan) * L.slot_bytes
+
+
+def test_split_signal_count_matches_kernel_grid():
+    """The count each rank adds per chunk is the strided split's grid size, the
+    value the GEMM's wait targets are built from."""
+    from fp_emulation import _lib
+
+    lib = _lib.load()
+    for rows, k in [(1, 1), (32, 128), (33, 129), (256, 16384), (255, 8192), (60, 700)]:
+        res_ld = (k + 15) // 16 * 16
+        assert lib.fpemu_split_mc_signals(rows, k) == -(-rows // 32) * -(-res_ld // 128)
