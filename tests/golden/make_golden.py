@@ -4,11 +4,12 @@ Run in the build container, where the read-only reference tree exists:
 
     python tests/golden/make_golden.py
 
-It imports thezettascale/fp-emulation from ``/root/reference/src`` (its CPU
-path JIT-builds ``crt_reconstruct.cpp``; ``LIBRARY_PATH`` gets gcc's libdir so
-``-lgomp`` links, and the JIT cache goes under the repo's ``_work/``), runs the
-stage functions of ``ozaki.py`` on seeded inputs and saves inputs, every stage
-output and the final result as ``tests/golden/*.npz``.  Large stage tensors are
+It imports thezettascale/fp-emulation from the reference source tree named by
+``REF_SRC`` below (its CPU path JIT-builds ``crt_reconstruct.cpp``;
+``LIBRARY_PATH`` gets gcc's libdir so ``-lgomp`` links, and the JIT cache goes
+under ``oracle/_build/torch_ext``, git-ignored), runs the stage functions of
+``ozaki.py`` on seeded inputs and saves inputs, every stage output and the
+final result as ``tests/golden/*.npz``.  Large stage tensors are
 stored as SHA-256 digests plus a few sampled planes to keep the fixtures small.
 
 The fixtures pin the oracle (``oracle/ozaki_oracle.py``) to the reference
@@ -33,7 +34,7 @@ FULL_LIMIT = 40_000
 
 def _setup_reference():
     os.environ["LIBRARY_PATH"] = "/usr/lib/gcc/x86_64-linux-gnu/13:" + os.environ.get("LIBRARY_PATH", "")
-    os.environ.setdefault("TORCH_EXTENSIONS_DIR", str(REPO / "_work" / "torch_ext"))
+    os.environ.setdefault("TORCH_EXTENSIONS_DIR", str(REPO / "oracle" / "_build" / "torch_ext"))
     sys.path.insert(0, str(REF_SRC))
     import fp_emulation.ozaki as oz  # the reference package
 
