@@ -160,6 +160,28 @@ def test_odd_shapes_bit_exact_vs_oracle(torch_cuda, m, k, n):
     np.testing.assert_array_equal(got.view(np.int64), want.view(np.int64))
 
 
+def test_k_at_the_int32_accumulation_limit(torch_cuda):
+    """k = 214748, the largest inner dimension whose per-modulus int32 sums stay
+    exact at n_mod = 25 (k * 100^2 < 2^31), is bit-exact against the oracle;
+    one more is refused (the reference's int32 GEMM would overflow silently)."""
+    torch = torch_cuda
+    from fp_emulation import _lib, ozaki2_int8_matmul
+
+    lib = _lib.load()
+    kmax = lib.fpemu_max_k(25)
+    assert kmax == 214748 and oo.n_moduli(kmax, 53) == 25
+    rng = np.random.default_rng(5)
+    A = (rng.random((3, kmax)) - 0.5) * np.exp(rng.standard_normal((3, kmax)))
+    B = (rng.random((kmax, 2)) - 0.5) * np.exp(rng.standard_normal((kmax, 2)))
+    A[:, :7] = 0.5  # residues near p-1 in many columns: large per-modulus sums
+    want = oo.ozaki2_matmul(A, B)
+    got = ozaki2_int8_matmul(_cuda(torch, A), _cuda(torch, B)).cpu().numpy()
+    np.testing.assert_array_equal(got.view(np.int64), want.view(np.int64))
+    with pytest.raises(_lib.FpemuError, match="int32"):
+        ozaki2_int8_matmul(torch.ones(2, kmax + 1, dtype=torch.float64, device="cuda"),
+                           torch.ones(kmax + 1, 2, dtype=torch.float64, device="cuda"))
+
+
 def test_transposed_and_strided_views(torch_cuda):
     """A and B given as transposed / sliced views: no copies, same bits."""
     torch = torch_cuda
