@@ -78,17 +78,18 @@ class _IpcChunks:
         serial = _IpcChunks._serials.get(members, 0)
         _IpcChunks._serials[members] = serial + 1
         self.key_prefix = f"fpemu_ce/{'-'.join(map(str, members))}/{serial}"
-        flags = rt.cudaEventDisableTiming | rt.cudaEventInterprocess
-        with torch.cuda.device(device):
+        R = self._rt
+        flags = R.cudaEventDisableTiming | R.cudaEventInterprocess
+        with self._device_ctx():
             self.nbytes = chunk_bytes * n_chunks
-            self.ptr = _check(rt.cudaMalloc(self.nbytes), "cudaMalloc")
-            self.buf = torch.as_tensor(_Ext(int(self.ptr), self.nbytes), device=device)
-            self.ev = {name: [_check(rt.cudaEventCreateWithFlags(flags), "cudaEventCreate")
+            self.ptr = _check(R.cudaMalloc(self.nbytes), "cudaMalloc")
+            self.buf = self._wrap_buffer(int(self.ptr), self.nbytes)
+            self.ev = {name: [_check(R.cudaEventCreateWithFlags(flags), "cudaEventCreate")
                               for _ in range(self._events_per_chunk(name) * n_chunks)]
                        for name in self.EVENTS}
-            self.gemm_done = [torch.cuda.Event() for _ in range(n_chunks)]
-            mem_h = bytes(_check(rt.cudaIpcGetMemHandle(self.ptr), "cudaIpcGetMemHandle").reserved)
-            ev_h = {name: [bytes(_check(rt.cudaIpcGetEventHandle(e), "cudaIpcGetEventHandle").reserved)
+            self.gemm_done = [self._local_event() for _ in range(n_chunks)]
+            mem_h = bytes(_check(R.cudaIpcGetMemHandle(self.ptr), "cudaIpcGetMemHandle").reserved)
+            ev_h = {name: [bytes(_check(R.cudaIpcGetEventHandle(e), "cudaIpcGetEventHandle").reserved)
                            for e in evs] for name, evs in self.ev.items()}
         self._table = [None] * self.world
         dist.all_gather_object(self._table, (mem_h, ev_h), group=group)
@@ -99,23 +100,45 @@ class _IpcChunks:
     def _events_per_chunk(self, name):
         return 1
 
+    # -- the CUDA runtime and torch objects this class touches.  Kept behind
+    # these hooks so that the enqueue protocol can be exercised on the CPU with
+    # a fake runtime (tests/test_ce_protocol.py); the defaults are the real ones.
+    _rt = rt
+
+    def _device_ctx(self):
+        return torch.cuda.device(self.device)
+
+    def _wrap_buffer(self, ptr, nbytes):
+        return torch.as_tensor(_Ext(ptr, nbytes), device=self.device)
+
+    def _local_event(self):
+        return torch.cuda.Event()
+
+    def _new_stream(self):
+        return torch.cuda.Stream(self.device)
+
+    def _current_stream(self):
+        return torch.cuda.current_stream(self.device)
+
     def peer_ptr(self, r):
         if r not in self._peer_ptr:
-            h = rt.cudaIpcMemHandle_t()
+            R = self._rt
+            h = R.cudaIpcMemHandle_t()
             h.reserved = self._table[r][0]
-            with torch.cuda.device(self.device):
-                self._peer_ptr[r] = int(_check(rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess),
+            with self._device_ctx():
+                self._peer_ptr[r] = int(_check(R.cudaIpcOpenMemHandle(h, R.cudaIpcMemLazyEnablePeerAccess),
                                                "cudaIpcOpenMemHandle"))
         return self._peer_ptr[r]
 
     def peer_events(self, r, name):
         if (r, name) not in self._peer_ev:
+            R = self._rt
             evs = []
-            with torch.cuda.device(self.device):
+            with self._device_ctx():
                 for hb in self._table[r][1][name]:
-                    eh = rt.cudaIpcEventHandle_t()
+                    eh = R.cudaIpcEventHandle_t()
                     eh.reserved = hb
-                    evs.append(_check(rt.cudaIpcOpenEventHandle(eh), "cudaIpcOpenEventHandle"))
+                    evs.append(_check(R.cudaIpcOpenEventHandle(eh), "cudaIpcOpenEventHandle"))
             self._peer_ev[(r, name)] = evs
         return self._peer_ev[(r, name)]
 
@@ -139,18 +162,15 @@ class _IpcChunks:
             for ph in phases:
                 self.store.delete_key(self._key(self.rank, call, ph))
 
-    @staticmethod
-    def _wait(stream, event, what="wait"):
-        _check(rt.cudaStreamWaitEvent(stream.cuda_stream, event, 0), what)
+    def _wait(self, stream, event, what="wait"):
+        _check(self._rt.cudaStreamWaitEvent(stream.cuda_stream, event, 0), what)
 
-    @staticmethod
-    def _record(stream, event):
-        _check(rt.cudaEventRecord(event, stream.cuda_stream), "record")
+    def _record(self, stream, event):
+        _check(self._rt.cudaEventRecord(event, stream.cuda_stream), "record")
 
-    @staticmethod
-    def _copy(stream, dst, src, nbytes):
-        _check(rt.cudaMemcpyAsync(dst, src, nbytes, rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice,
-                                  stream.cuda_stream), "memcpy")
+    def _copy(self, stream, dst, src, nbytes):
+        _check(self._rt.cudaMemcpyAsync(dst, src, nbytes, self._rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice,
+                                        stream.cuda_stream), "memcpy")
 
     def after_gemm(self, c, stream):
         """This rank's GEMM on chunk c is enqueued on `stream`: the chunk may be
@@ -160,7 +180,7 @@ class _IpcChunks:
     def close(self):
         for ptr in self._peer_ptr.values():
             try:
-                rt.cudaIpcCloseMemHandle(ptr)
+                self._rt.cudaIpcCloseMemHandle(ptr)
             except Exception:
                 pass
         self._peer_ptr = {}
@@ -183,8 +203,8 @@ class CeChain(_IpcChunks):
         pos = order.index(self.rank)
         self.pred = order[pos - 1] if pos > 0 else None
         self.succ = order[pos + 1] if pos + 1 < self.world else None
-        self.split_stream = torch.cuda.current_stream(device)
-        self.copy_stream = torch.cuda.Stream(device)
+        self.split_stream = self._current_stream()
+        self.copy_stream = self._new_stream()
 
     def _events_per_chunk(self, name):
         return self.pieces
@@ -198,9 +218,16 @@ class CeChain(_IpcChunks):
         lo = min(q * step, self.chunk_bytes)
         return lo, min(self.chunk_bytes, lo + step)
 
+    # Store keys of old calls: key (r, i) is waited on by r's successor in call i
+    # and by r's predecessor in call i+1.  When r has passed its own key waits of
+    # call i+2 -- its predecessor's key of i+2 and its successor's of i+1, each
+    # published after that rank's waits of the earlier call -- both neighbours
+    # are done with (r, i), so r deletes it then.
+
     def root_begin(self, main_stream):
         if self.calls > 0 and self.succ is not None:
             self._wait_keys([self.succ], self.calls - 1, "A")
+        self._forget(self.calls - 2, ("A",))
         self.split_stream = main_stream
 
     def root_before_write(self, c):
@@ -221,6 +248,7 @@ class CeChain(_IpcChunks):
         if i > 0 and self.succ is not None:
             self._wait_keys([self.succ], i - 1, "A")
         self._wait_keys([self.pred], i, "A")
+        self._forget(i - 2, ("A",))
         cs = self.copy_stream
         pred_ptr = self.peer_ptr(self.pred)
         for c in range(self.n_chunks):

@@ -1,0 +1,201 @@
+"""The copy-engine chain's enqueue protocol (fp_emulation/ce_transport.py) on
+CPU ranks (gloo, one process per rank), with a fake CUDA runtime.
+
+A stream may wait on a peer's interprocess event only after the peer has
+enqueued the matching record -- and before it enqueues the next one, or the
+wait binds to the wrong call.  The fake runtime counts every record of every
+event in the process group's store at the moment it is enqueued, and logs, for
+every stream wait, the count it saw.  The protocol is right when, in call i,
+each wait on the predecessor's ``done`` saw exactly i+1 records (this call's),
+each wait on the successor's ``done`` exactly i (the previous call's: the
+successor has read it, and not yet begun the next), and each wait on the rank's
+own ``done`` exactly i+1 -- for 2 to 4 ranks, roots other than rank 0, and
+several calls in a row.  Old store keys must be deleted as calls go by.
+"""
+from __future__ import annotations
+
+import contextlib
+import os
+import socket
+import traceback
+from datetime import timedelta
+
+import pytest
+import torch.multiprocessing as mp
+
+from cuda.bindings import runtime as _real_rt
+
+OK = _real_rt.cudaError_t.cudaSuccess
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+class _Handle:
+    def __init__(self, reserved=b""):
+        self.reserved = reserved
+
+
+class FakeRt:
+    """The runtime calls the transport makes, recorded instead of executed."""
+
+    cudaEventDisableTiming = 2
+    cudaEventInterprocess = 4
+    cudaIpcMemLazyEnablePeerAccess = 1
+    cudaIpcMemHandle_t = _Handle
+    cudaIpcEventHandle_t = _Handle
+
+    class cudaMemcpyKind:
+        cudaMemcpyDeviceToDevice = 3
+
+    def __init__(self, rank, store):
+        self.rank, self.store = rank, store
+        self.n_events = 0
+        self.chain = None
+        self.waits = []   # (owner, event index, records seen, chain.calls at the wait)
+        self.copies = 0
+
+    def _rec_key(self, ev):
+        return f"fake_rec/{ev[0]}/{ev[1]}"
+
+    def cudaMalloc(self, nbytes):
+        return OK, 0x10000000 * (self.rank + 1)
+
+    def cudaEventCreateWithFlags(self, flags):
+        self.n_events += 1
+        return OK, (self.rank, self.n_events - 1)
+
+    def cudaIpcGetMemHandle(self, ptr):
+        return OK, _Handle(f"mem{self.rank}".encode())
+
+    def cudaIpcGetEventHandle(self, ev):
+        return OK, _Handle(f"{ev[0]}:{ev[1]}".encode())
+
+    def cudaIpcOpenMemHandle(self, h, flags):
+        return OK, 0x10000000 * (int(h.reserved.decode()[3:]) + 1)
+
+    def cudaIpcOpenEventHandle(self, h):
+        owner, idx = h.reserved.decode().split(":")
+        return OK, (int(owner), int(idx))
+
+    def cudaIpcCloseMemHandle(self, ptr):
+        return (OK,)
+
+    def cudaEventRecord(self, ev, stream):
+        self.store.add(self._rec_key(ev), 1)
+        return (OK,)
+
+    def cudaStreamWaitEvent(self, stream, ev, flags):
+        seen = self.store.add(self._rec_key(ev), 0)
+        self.waits.append((ev[0], ev[1], seen, self.chain.calls))
+        return (OK,)
+
+    def cudaMemcpyAsync(self, dst, src, nbytes, kind, stream):
+        self.copies += 1
+        return (OK,)
+
+
+class _Stream:
+    cuda_stream = 0
+
+    def wait_event(self, ev):
+        pass
+
+
+class _LocalEvent:
+    def record(self, stream=None):
+        pass
+
+
+def _worker(rank, world, port, root, calls, pieces, n_chunks, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        from fp_emulation import ce_transport as ct
+
+        store = dist.distributed_c10d._get_default_store()
+        fake = FakeRt(rank, store)
+
+        class FakeChain(ct.CeChain):
+            _rt = fake
+
+            def _device_ctx(self):
+                return contextlib.nullcontext()
+
+            def _wrap_buffer(self, ptr, nbytes):
+                return None
+
+            def _local_event(self):
+                return _LocalEvent()
+
+            def _new_stream(self):
+                return _Stream()
+
+            def _current_stream(self):
+                return _Stream()
+
+        chain = FakeChain(None, root, None, chunk_bytes=4096, n_chunks=n_chunks, pieces=pieces)
+        fake.chain = chain
+        main = _Stream()
+        # The call sequence of distributed.rowsharded_product_ce, without data.
+        for _ in range(calls):
+            if rank == root:
+                chain.root_begin(main)
+                for c in range(n_chunks):
+                    chain.root_before_write(c)
+                    chain.root_after_write(c)
+                chain.root_end()
+            else:
+                chain.pull()
+            for c in range(n_chunks):
+                chain.wait_chunk(c, main)
+                chain.after_gemm(c, main)
+        dist.barrier()
+        left = [i for i in range(calls) if store.check([chain._key(rank, i, "A")])]
+        q.put((rank, "ok", (chain.pred, chain.succ, fake.waits, fake.copies, left)))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, "error", traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world,root", [(2, 0), (3, 1), (4, 2)])
+def test_chain_waits_bind_to_the_right_records(world, root):
+    calls, pieces, n_chunks = 4, 3, 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, root, calls, pieces, n_chunks, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=180) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    per_chunk = n_chunks * pieces
+    for rank, status, payload in results:
+        assert status == "ok", payload
+        pred, succ, waits, copies, left = payload
+        n_pred = n_succ = n_own = 0
+        for owner, _idx, seen, at_call in waits:
+            if owner == rank:        # wait_chunk, after this call's records
+                assert seen == at_call, (rank, owner, seen, at_call)
+                n_own += 1
+            elif owner == pred:      # this call's records of the predecessor
+                assert seen == at_call + 1, (rank, owner, seen, at_call)
+                n_pred += 1
+            elif owner == succ:      # the successor's reads of the previous call
+                assert seen == at_call, (rank, owner, seen, at_call)
+                n_succ += 1
+            else:
+                raise AssertionError(f"rank {rank} waited on rank {owner}'s event")
+        assert n_own == calls * n_chunks
+        assert n_pred == (0 if rank == root else calls * per_chunk)
+        assert n_succ == (0 if succ is None else (calls - 1) * per_chunk)
+        assert copies == (0 if rank == root else calls * per_chunk)
+        assert left == [calls - 2, calls - 1], left  # older keys were deleted
