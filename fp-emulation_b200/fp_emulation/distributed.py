@@ -19,7 +19,6 @@ same pipeline can be exercised with CPU ranks over gloo in tests.
 """
 from __future__ import annotations
 
-import ctypes
 import os
 import warnings
 from dataclasses import dataclass
