@@ -365,6 +365,8 @@ def run_ours(args):
     # wait + a signal beside its staging copies.
     if world == 1:
         per_rank = 4
+    elif transport_used == "ce-ring":
+        per_rank = 1 + 3 * n_chunks
     elif transport_used == "nvls":
         per_rank = 1 + 7 * n_chunks + (2 * n_chunks if rank == root else 0)
     else:

@@ -64,7 +64,7 @@ class _IpcChunks:
     _serials: dict = {}
     EVENTS: tuple = ()
 
-    def __init__(self, group, root, device, chunk_bytes, n_chunks):
+    def __init__(self, group, root, device, chunk_bytes, n_chunks, extra_bytes=0):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -81,7 +81,7 @@ class _IpcChunks:
         R = self._rt
         flags = R.cudaEventDisableTiming | R.cudaEventInterprocess
         with self._device_ctx():
-            self.nbytes = chunk_bytes * n_chunks
+            self.nbytes = chunk_bytes * n_chunks + extra_bytes
             self.ptr = _check(R.cudaMalloc(self.nbytes), "cudaMalloc")
             self.buf = self._wrap_buffer(int(self.ptr), self.nbytes)
             self.ev = {name: [_check(R.cudaEventCreateWithFlags(flags), "cudaEventCreate")
@@ -171,6 +171,11 @@ class _IpcChunks:
     def _copy(self, stream, dst, src, nbytes):
         _check(self._rt.cudaMemcpyAsync(dst, src, nbytes, self._rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice,
                                         stream.cuda_stream), "memcpy")
+
+    def _copy2d(self, stream, dst, dpitch, src, spitch, width, height):
+        _check(self._rt.cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height,
+                                          self._rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice, stream.cuda_stream),
+               "memcpy2d")
 
     def after_gemm(self, c, stream):
         """This rank's GEMM on chunk c is enqueued on `stream`: the chunk may be
@@ -269,4 +274,146 @@ class CeChain(_IpcChunks):
         self._wait(stream, self._done(self.rank, c, self.pieces - 1), "wait chunk")
 
 
-TRANSPORTS = {"ce": CeChain}
+class CeRing(_IpcChunks):
+    """Every rank splits one strip of each chunk; the residue strips then go
+    round a ring by the copy engines.  Opt-in: bit-exact on 2 GPUs, not yet
+    measured or run on more (its enqueue protocol is checked on 2-4 CPU ranks
+    with a fake runtime).
+
+    Ranks form the ring order = root, root+1, ...; pred/succ are the neighbours
+    in it.  Per call and chunk c:
+      root, copy stream:    FP64 strip q of B -> rank q's staging slot c (2-D copy
+                            into the peer's buffer), then record stage[c];
+      rank r, split stream: wait the root's stage[c], split its own strip into
+                            its residue buffer, record have[c][r];
+      rank r, ring step t (1 .. W-1, one stream per step): the strip s that is t
+                            positions behind r in the ring is in pred's buffer
+                            once pred's have[c][s] fires (pred's own split for
+                            t = 1, its step t-1 otherwise): copy it, record
+                            have[c][s];
+      GEMM on chunk c:      after have[c][q] for every q.
+    Reuse across calls: the root overwrites slot c after every rank's split of
+    the previous call read it (have[c][q] on rank q); r overwrites its strip s
+    of chunk c after its own GEMM of the previous call and, unless s is succ's
+    own strip, after succ pulled it (succ's have[c][s]).
+    Host phases, each published as a key once its records are enqueued: "stage"
+    (root), "split", "ring1" .. "ring{W-1}"; before enqueuing a wait, a rank
+    waits for the key of the phase that enqueued the matching record.  Every
+    dependency points to an earlier phase of the same call or to the previous
+    call, so the phases never wait in a circle, and a stream wait always binds
+    to the intended record: the peer cannot enqueue its next record of that
+    event before the waiting rank has published the phase holding the wait."""
+
+    EVENTS = ("stage", "have")
+
+    def __init__(self, group, root, device, layout):
+        self.layout = layout
+        nc = len(layout.plan)
+        super().__init__(group, root, device, layout.chunk_bytes, nc, extra_bytes=nc * layout.slot_bytes)
+        W = self.world
+        self.order = [(root + i) % W for i in range(W)]
+        self.pos = self.order.index(self.rank)
+        self.pred = self.order[(self.pos - 1) % W]
+        self.succ = self.order[(self.pos + 1) % W]
+        self.split_stream = self._new_stream()
+        self.copy_stream = self._new_stream()
+        self.ring = [self._new_stream() for _ in range(W - 1)]  # step t on ring[t - 1]
+        self.phases = ("stage", "split") + tuple(f"ring{t}" for t in range(1, W))
+
+    def _events_per_chunk(self, name):
+        return self.world if name == "have" else 1
+
+    def _have(self, owner, c, q):
+        evs = self.ev["have"] if owner == self.rank else self.peer_events(owner, "have")
+        return evs[c * self.world + q]
+
+    def _stage(self, c):
+        evs = self.ev["stage"] if self.rank == self.root else self.peer_events(self.root, "stage")
+        return evs[c]
+
+    def strip_at(self, t):
+        """The strip (by owning rank) that reaches this rank at ring step t."""
+        return self.order[(self.pos - t) % self.world]
+
+    def _base(self, r):
+        return int(self.ptr) if r == self.rank else self.peer_ptr(r)
+
+    # -- per call ---------------------------------------------------------------
+    def root_stage(self, B_ptr, ldb, main_stream):
+        """Root: FP64 strips of every chunk into every rank's staging slots.
+        B_ptr/ldb: the root's B (row-major, ldb doubles per row)."""
+        i = self.calls
+        L = self.layout
+        if i > 0:
+            self._wait_keys(self.order, i - 1, "split")
+        cs = self.copy_stream
+        cs.wait_stream(main_stream)
+        for c, (c0, _c1) in enumerate(L.plan):
+            if i > 0:
+                for q in range(self.world):
+                    self._wait(cs, self._have(q, c, q), "stage war")
+            for q, (s0, s1) in enumerate(L.strips[c]):
+                if s1 > s0:
+                    self._copy2d(cs, self._base(q) + L.stage_off + c * L.slot_bytes, L.pitch * 8,
+                                 B_ptr + (c0 + s0) * 8, ldb * 8, (s1 - s0) * 8, L.k)
+            self._record(cs, self._stage(c))
+        self._publish("stage")
+
+    def split_own(self, split_fn):
+        """Every rank: split_fn(c, stream) enqueues on `stream` the split of this
+        rank's FP64 strip of chunk c (staging slot c) into its residue strip."""
+        i = self.calls
+        self._wait_keys([self.root], i, "stage")
+        if i > 0 and self.world > 1:
+            self._wait_keys([self.succ], i - 1, "ring1")
+        ss = self.split_stream
+        for c in range(len(self.layout.plan)):
+            ss.wait_event(self.gemm_done[c])
+            self._wait(ss, self._stage(c), "stage")
+            if i > 0 and self.world > 1:  # succ pulled this strip at its step 1
+                self._wait(ss, self._have(self.succ, c, self.rank), "split war")
+            split_fn(c, ss)
+            self._record(ss, self._have(self.rank, c, self.rank))
+        self._publish("split")
+
+    def ring_steps(self):
+        """Every rank: pull the W-1 other strips of every chunk round the ring."""
+        i = self.calls
+        L = self.layout
+        W = self.world
+        for t in range(1, W):
+            self._wait_keys([self.pred], i, "split" if t == 1 else f"ring{t - 1}")
+            war = i > 0 and t < W - 1  # succ pulls this strip from us at its step t+1
+            if war:
+                self._wait_keys([self.succ], i - 1, f"ring{t + 1}")
+            rs = self.ring[t - 1]
+            s = self.strip_at(t)
+            for c, (c0, c1) in enumerate(L.plan):
+                rs.wait_event(self.gemm_done[c])
+                self._wait(rs, self._have(self.pred, c, s), "ring")
+                if war:
+                    self._wait(rs, self._have(self.succ, c, s), "ring war")
+                s0, s1 = L.strips[c][s]
+                if s1 > s0:
+                    w = c1 - c0
+                    base = c * L.chunk_bytes
+                    # residues: rows s0..s1 of each of the n_mod planes (plane stride w*ld)
+                    self._copy2d(rs, int(self.ptr) + base + s0 * L.ld, w * L.ld,
+                                 self.peer_ptr(self.pred) + base + s0 * L.ld, w * L.ld, (s1 - s0) * L.ld, L.n_mod)
+                    off = base + L.res_bytes + 4 * s0  # column exponents
+                    self._copy(rs, int(self.ptr) + off, self.peer_ptr(self.pred) + off, 4 * (s1 - s0))
+                self._record(rs, self._have(self.rank, c, s))
+            self._publish(f"ring{t}")
+        # Every rank that waits on this rank's keys of call i-2 has passed those
+        # waits (they sit in calls i-2 and i-1 of the neighbours and the root,
+        # whose later keys this rank has just waited for).
+        self._forget(i - 2, self.phases)
+        self.calls += 1
+
+    def wait_chunk(self, c, stream):
+        """`stream` waits until every strip of chunk c is in this rank's buffer."""
+        for q in range(self.world):
+            self._wait(stream, self._have(self.rank, c, q), "gemm")
+
+
+TRANSPORTS = {"ce": CeChain, "ce-ring": CeRing}

@@ -46,6 +46,9 @@ BCAST_MODE = os.environ.get("FPEMU_BCAST", "residues")
 #         "ce" where the group has no multicast support.  Opt-in: measured slower
 #         than "ce" at 8 GPUs (the multicast splits slow the concurrent GEMMs),
 #         and its counter waits timed out when a chunk's GEMM grid covered every SM;
+#  "ce-ring": every rank splits a strip of each chunk (FP64 strips copied from the
+#         root), the residue strips go round a ring by the copy engines
+#         (ce_transport.CeRing); bit-exact on 2 GPUs, not yet measured;
 #  "nccl": the root splits B, NCCL broadcast kernels move the chunks.
 TRANSPORT = os.environ.get("FPEMU_TRANSPORT", "ce")
 
@@ -193,6 +196,61 @@ class _NvlsSetupError(RuntimeError):
     pass
 
 
+def rowsharded_product_ring(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, chunk_cols=CHUNK_COLS):
+    """Same product through the copy-engine ring (ce_transport.CeRing): the root
+    copies each rank its FP64 strip of every chunk, every rank splits its strip,
+    and the residue strips go round the ring by the copy engines.  Opt-in
+    (FPEMU_TRANSPORT=ce-ring): bit-exact on 2 GPUs, not yet measured."""
+    from fp_emulation.ce_transport import CeRing
+    from fp_emulation.strips import StripLayout
+
+    rank = dist.get_rank(group)
+    dev = A_local.device
+    m = A_local.shape[0]
+    ld = _res_ld(k)
+    plan = plan_column_chunks(n, chunk_cols)
+    key = ("ce-ring", id(group), root, dev.index, k, n, n_mod, tuple(plan))
+    tr = _TRANSPORTS.get(key)
+    if tr is None:
+        tr = _TRANSPORTS[key] = CeRing(group, root, dev, StripLayout(dist.get_world_size(group), k, n_mod, ld, plan))
+    L = tr.layout
+    stream = torch.cuda.current_stream(dev)
+
+    def views(c):
+        w = plan[c][1] - plan[c][0]
+        blk = tr.chunk_view(c)
+        return blk[: n_mod * w * ld].view(n_mod, w, ld), blk[L.res_bytes: L.res_bytes + 4 * w].view(torch.int32)
+
+    if rank == root:
+        Bc = B if B.stride(1) == 1 else B.contiguous()
+        Bc.record_stream(tr.copy_stream)
+        tr.root_stage(Bc.data_ptr(), Bc.stride(0), stream)
+
+    def split_fn(c, ss):
+        s0, s1 = L.strips[c][rank]
+        if s1 == s0:
+            return
+        res, exps = views(c)
+        slot = tr.buf[L.stage_off + c * L.slot_bytes: L.stage_off + c * L.slot_bytes + 8 * k * L.pitch]
+        X = slot.view(torch.float64).view(k, L.pitch)[:, : s1 - s0].T  # strip's columns as rows, K strided
+        with torch.cuda.stream(ss):
+            ops.split(X, bits, n_mod, res[:, s0:s1, :], exps[s0:s1])
+
+    tr.split_own(split_fn)
+    tr.ring_steps()
+    a_res = ops.empty_res(n_mod, m, ld)
+    row_exp = ops.empty_exps(m)
+    ops.split(A_local, bits, n_mod, a_res, row_exp)
+    C = torch.empty((m, n), dtype=torch.float64, device=dev)
+    for c, (c0, c1) in enumerate(plan):
+        res, exps = views(c)
+        tr.wait_chunk(c, stream)
+        if m and c1 > c0:
+            ops.gemm_crt(a_res, row_exp, res, exps, bits, C, c0, c1, k)
+        tr.after_gemm(c, stream)
+    return C
+
+
 _NVLS_OK = {}
 
 
@@ -202,6 +260,8 @@ def rowsharded_product_auto(A_local, B, n, k, bits, n_mod, ops, root=0, group=No
     kind = transport or TRANSPORT
     if BCAST_MODE != "residues" or kind == "nccl":
         return rowsharded_product(A_local, B, n, k, bits, n_mod, ops, root, group)
+    if kind == "ce-ring":
+        return rowsharded_product_ring(A_local, B, n, k, bits, n_mod, ops, root, group)
     if kind == "nvls":
         gkey = id(group)
         if gkey not in _NVLS_OK:

@@ -1,0 +1,65 @@
+"""Column strips of B's chunks and the byte layout of the per-GPU buffer that
+holds them, shared by the transports in which every GPU splits one strip of
+each chunk (nvls_transport.py, and the copy-engine ring in ce_transport.py)."""
+from __future__ import annotations
+
+
+def _align256(x):
+    return (x + 255) // 256 * 256
+
+
+def _even_split(w, parts, i):
+    """Columns [s0, s1) of part i when w columns are cut into `parts` near-equal strips."""
+    base, extra = divmod(w, parts)
+    s0 = i * base + min(i, extra)
+    return s0, s0 + base + (1 if i < extra else 0)
+
+
+class StripLayout:
+    """Byte layout of a GPU's buffer for one (world, k, n_mod, ld, plan):
+    [chunk 0 .. chunk nc-1 | staging slot 0 .. nc-1 | counters split/stage/gemm]
+    (the counters are the NVLS transport's; the ring transport stops before them).
+
+    chunk j: int8 residues [n_mod][w_j][ld] (plane stride w_j * ld), then the
+    w_j int32 column exponents at res_bytes; strip q of chunk j is columns
+    strips[j][q] of the chunk.  Staging slot j: rank's FP64 strip, k rows of
+    `pitch` doubles (pitch >= 2 keeps the split's K stride non-unit)."""
+
+    def __init__(self, world, k, n_mod, ld, plan):
+        self.world, self.k, self.n_mod, self.ld, self.plan = world, k, n_mod, ld, plan
+        nc = len(plan)
+        self.strips = [[_even_split(c1 - c0, world, q) for q in range(world)] for c0, c1 in plan]
+        wmax = max(c1 - c0 for c0, c1 in plan)
+        swmax = max(s1 - s0 for row in self.strips for s0, s1 in row)
+        self.swmax = swmax
+        self.pitch = max(swmax, 2)
+        self.res_bytes = _align256(n_mod * wmax * ld)
+        self.chunk_bytes = self.res_bytes + _align256(wmax * 4)
+        self.slot_bytes = _align256(k * self.pitch * 8)
+        self.stage_off = nc * self.chunk_bytes
+        self.cnt_off = self.stage_off + nc * self.slot_bytes
+        self.total = self.cnt_off + _align256(3 * nc * 8)
+
+    def counter(self, kind, j):
+        return self.cnt_off + 8 * (kind * len(self.plan) + j)
+
+    def residue_span(self, j, q):
+        """[first, last] byte offsets the split of strip q of chunk j writes
+        (residues), and the same for its exponents; None for an empty strip."""
+        c0, c1 = self.plan[j]
+        w = c1 - c0
+        s0, s1 = self.strips[j][q]
+        if s1 == s0:
+            return None
+        base = j * self.chunk_bytes
+        res = (base + s0 * self.ld, base + (self.n_mod - 1) * w * self.ld + (s1 - 1) * self.ld + self.ld - 1)
+        exps = (base + self.res_bytes + 4 * s0, base + self.res_bytes + 4 * s1 - 1)
+        return res, exps
+
+    def staging_span(self, j, q):
+        """[first, last] byte offsets the 2-D copy of strip q fills in slot j."""
+        s0, s1 = self.strips[j][q]
+        if s1 == s0:
+            return None
+        base = self.stage_off + j * self.slot_bytes
+        return base, base + (self.k - 1) * self.pitch * 8 + (s1 - s0) * 8 - 1

@@ -55,8 +55,10 @@ class FakeRt:
         self.rank, self.store = rank, store
         self.n_events = 0
         self.chain = None
-        self.waits = []   # (owner, event index, records seen, chain.calls at the wait)
+        self.waits = []   # (owner, event index, records seen, chain.calls at the wait, label)
         self.copies = 0
+        self.copies2d = 0
+        self.label = ""
 
     def _rec_key(self, ev):
         return f"fake_rec/{ev[0]}/{ev[1]}"
@@ -90,11 +92,16 @@ class FakeRt:
 
     def cudaStreamWaitEvent(self, stream, ev, flags):
         seen = self.store.add(self._rec_key(ev), 0)
-        self.waits.append((ev[0], ev[1], seen, self.chain.calls))
+        self.waits.append((ev[0], ev[1], seen, self.chain.calls, self.label))
         return (OK,)
 
     def cudaMemcpyAsync(self, dst, src, nbytes, kind, stream):
         self.copies += 1
+        return (OK,)
+
+    def cudaMemcpy2DAsync(self, dst, dpitch, src, spitch, width, height, kind, stream):
+        assert width <= dpitch and width <= spitch and height >= 1
+        self.copies2d += 1
         return (OK,)
 
 
@@ -102,6 +109,9 @@ class _Stream:
     cuda_stream = 0
 
     def wait_event(self, ev):
+        pass
+
+    def wait_stream(self, other):
         pass
 
 
@@ -182,7 +192,7 @@ def test_chain_waits_bind_to_the_right_records(world, root):
         assert status == "ok", payload
         pred, succ, waits, copies, left = payload
         n_pred = n_succ = n_own = 0
-        for owner, _idx, seen, at_call in waits:
+        for owner, _idx, seen, at_call, _label in waits:
             if owner == rank:        # wait_chunk, after this call's records
                 assert seen == at_call, (rank, owner, seen, at_call)
                 n_own += 1
@@ -199,3 +209,109 @@ def test_chain_waits_bind_to_the_right_records(world, root):
         assert n_succ == (0 if succ is None else (calls - 1) * per_chunk)
         assert copies == (0 if rank == root else calls * per_chunk)
         assert left == [calls - 2, calls - 1], left  # older keys were deleted
+
+
+# -- the ring: every rank splits a strip, strips go round the ring --------------
+
+# Which call's record each labelled wait must bind to: "war" waits check that a
+# reader of the previous call is done (its record of call i-1: i records seen);
+# the others wait for data of this call (i+1 records).  GEMM waits come after
+# the call counter moved on, so they see exactly `calls` records.
+_PREVIOUS_CALL = {"stage war", "split war", "ring war", "gemm"}
+
+
+def _ring_worker(rank, world, port, root, calls, n_chunks, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        from fp_emulation import ce_transport as ct
+        from fp_emulation.distributed import plan_column_chunks
+        from fp_emulation.strips import StripLayout
+
+        store = dist.distributed_c10d._get_default_store()
+        fake = FakeRt(rank, store)
+
+        class FakeRing(ct.CeRing):
+            _rt = fake
+
+            def _device_ctx(self):
+                return contextlib.nullcontext()
+
+            def _wrap_buffer(self, ptr, nbytes):
+                return None
+
+            def _local_event(self):
+                return _LocalEvent()
+
+            def _new_stream(self):
+                return _Stream()
+
+            def _current_stream(self):
+                return _Stream()
+
+            def _wait(self, stream, event, what="wait"):
+                fake.label = what
+                return super()._wait(stream, event, what)
+
+        plan = plan_column_chunks(256 * n_chunks - 100, 256)  # a ragged last chunk
+        layout = StripLayout(world, 300, 24, 304, plan)
+        ring = FakeRing(None, root, None, layout)
+        fake.chain = ring
+        splits = []
+        main = _Stream()
+        for _ in range(calls):
+            if rank == root:
+                ring.root_stage(0x1000, 256 * n_chunks, main)
+            ring.split_own(lambda c, ss: splits.append(c))
+            ring.ring_steps()
+            for c in range(len(plan)):
+                ring.wait_chunk(c, main)
+                ring.after_gemm(c, main)
+        dist.barrier()
+        left = [i for i in range(calls) if store.check([ring._key(rank, i, "split")])]
+        q.put((rank, "ok", (ring.pred, ring.succ, fake.waits, fake.copies, fake.copies2d, len(splits), left,
+                            len(plan))))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, "error", traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world,root", [(2, 1), (3, 0), (4, 3)])
+def test_ring_waits_bind_to_the_right_records(world, root):
+    calls, n_chunks = 4, 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ring_worker, args=(r, world, port, root, calls, n_chunks, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=180) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, status, payload in results:
+        assert status == "ok", payload
+        pred, succ, waits, copies, copies2d, n_splits, left, nc = payload
+        counts = {}
+        for owner, _idx, seen, at_call, label in waits:
+            want = at_call if label in _PREVIOUS_CALL else at_call + 1
+            assert seen == want, (rank, owner, label, seen, at_call)
+            if label in ("ring", "ring war", "split war"):
+                assert owner == (pred if label == "ring" else succ), (rank, owner, label)
+            counts[label] = counts.get(label, 0) + 1
+        W = world
+        assert counts.get("stage war", 0) == (W * nc * (calls - 1) if rank == root else 0)
+        assert counts["stage"] == nc * calls
+        assert counts.get("split war", 0) == nc * (calls - 1)
+        assert counts["ring"] == (W - 1) * nc * calls
+        assert counts.get("ring war", 0) == (W - 2) * nc * (calls - 1)
+        assert counts["gemm"] == W * nc * calls
+        assert n_splits == nc * calls
+        # 2-D copies: the root's FP64 strips (W per chunk) and the ring's residue strips;
+        # 1-D copies: the ring's column exponents.
+        assert copies2d == (W * nc * calls if rank == root else 0) + (W - 1) * nc * calls
+        assert copies == (W - 1) * nc * calls
+        assert left == [calls - 2, calls - 1], left
