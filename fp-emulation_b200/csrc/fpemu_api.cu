@@ -577,6 +577,26 @@ int fpemu_split(int64_t rows, int64_t k, const double* X, int64_t s_row, int64_t
 
 // ------------------------------------------- multi-GPU (NVLS) primitives --
 
+// The kernels below run beside the persistent GEMM, and the waits may spin for a
+// while.  An SM's shared-memory carveout is fixed while blocks are resident, so a
+// small-carveout SM held by one of them could not host a GEMM CTA (which needs
+// ~193 KB); ask for the largest shared-memory carveout so they leave the SM in
+// a configuration the GEMM fits.  A scheduling preference, set once per device.
+static void prefer_max_shared_carveout() {
+    static std::mutex mu;
+    static bool done[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done[dev]) return;
+    const int carve = cudaSharedmemCarveoutMaxShared;
+    cudaFuncSetAttribute(wait_counters_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, carve);
+    cudaFuncSetAttribute(signal_counter_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, carve);
+    cudaFuncSetAttribute(split_strided_kernel<true>, cudaFuncAttributePreferredSharedMemoryCarveout, carve);
+    cudaGetLastError();  // a refused hint is not an error of the call
+    done[dev] = true;
+}
+
 int64_t fpemu_split_mc_signals(int64_t rows, int64_t k) {
     if (rows <= 0 || k < 1) return 0;
     const int64_t res_ld = res_ld_for(k);
@@ -622,6 +642,7 @@ int fpemu_split_mc(int64_t rows, int64_t k, const double* X, int64_t s_row, int6
     split_colmax_kernel<<<g1, 256, 0, st>>>(P, reinterpret_cast<unsigned long long*>(colmax_scratch));
     FPEMU_CUDA(cudaGetLastError());
     dim3 g2((unsigned)((rows + kTileR - 1) / kTileR), (unsigned)((res_ld + kTileK - 1) / kTileK));
+    prefer_max_shared_carveout();
     split_strided_kernel<true><<<g2, 256, 0, st>>>(P);
     FPEMU_CUDA(cudaGetLastError());
     return FPEMU_OK;
@@ -639,6 +660,7 @@ int fpemu_wait_counters(const uint64_t* const* counters, int n, uint64_t target,
         L.p[i] = reinterpret_cast<const unsigned long long*>(counters[i]);
     }
     L.n = n;
+    prefer_max_shared_carveout();
     wait_counters_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(L, (unsigned long long)target,
                                                                          (int64_t)wait_budget_ns(), where);
     FPEMU_CUDA(cudaGetLastError());
@@ -648,6 +670,7 @@ int fpemu_wait_counters(const uint64_t* const* counters, int n, uint64_t target,
 int fpemu_signal_counter(uint64_t* counter, int multicast, void* stream) {
     if (!counter || reinterpret_cast<uintptr_t>(counter) % 8 != 0)
         return fail(FPEMU_ERR_INVALID, "signal_counter: null or misaligned counter");
+    prefer_max_shared_carveout();
     signal_counter_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
         reinterpret_cast<unsigned long long*>(counter), multicast ? 1 : 0);
     FPEMU_CUDA(cudaGetLastError());
