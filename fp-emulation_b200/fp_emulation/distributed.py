@@ -217,9 +217,7 @@ def rowsharded_product_ring(A_local, B, n, k, bits, n_mod, ops, root=0, group=No
     stream = torch.cuda.current_stream(dev)
 
     def views(c):
-        w = plan[c][1] - plan[c][0]
-        blk = tr.chunk_view(c)
-        return blk[: n_mod * w * ld].view(n_mod, w, ld), blk[L.res_bytes: L.res_bytes + 4 * w].view(torch.int32)
+        return L.chunk_views(tr.buf, c)
 
     if rank == root:
         Bc = B if B.stride(1) == 1 else B.contiguous()
@@ -231,8 +229,7 @@ def rowsharded_product_ring(A_local, B, n, k, bits, n_mod, ops, root=0, group=No
         if s1 == s0:
             return
         res, exps = views(c)
-        slot = tr.buf[L.stage_off + c * L.slot_bytes: L.stage_off + c * L.slot_bytes + 8 * k * L.pitch]
-        X = slot.view(torch.float64).view(k, L.pitch)[:, : s1 - s0].T  # strip's columns as rows, K strided
+        X = L.staging_strip(tr.buf, c, rank)  # the strip's columns as rows, K strided
         with torch.cuda.stream(ss):
             ops.split(X, bits, n_mod, res[:, s0:s1, :], exps[s0:s1])
 

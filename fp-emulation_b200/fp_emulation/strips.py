@@ -3,6 +3,8 @@ holds them, shared by the transports in which every GPU splits one strip of
 each chunk (nvls_transport.py, and the copy-engine ring in ce_transport.py)."""
 from __future__ import annotations
 
+import torch
+
 
 def _align256(x):
     return (x + 255) // 256 * 256
@@ -63,3 +65,22 @@ class StripLayout:
             return None
         base = self.stage_off + j * self.slot_bytes
         return base, base + (self.k - 1) * self.pitch * 8 + (s1 - s0) * 8 - 1
+
+    # -- typed views of a GPU's buffer (a flat uint8 tensor laid out as above) --
+    def chunk_views(self, buf, j):
+        """(residues int8 [n_mod][w_j][ld], column exponents int32 [w_j]) of chunk j."""
+        c0, c1 = self.plan[j]
+        w = c1 - c0
+        blk = buf[j * self.chunk_bytes:(j + 1) * self.chunk_bytes]
+        return (blk[: self.n_mod * w * self.ld].view(self.n_mod, w, self.ld),
+                blk[self.res_bytes: self.res_bytes + 4 * w].view(torch.int32))
+
+    def staging_strip(self, buf, j, q):
+        """Strip q of chunk j as the split reads it from staging slot j: float64
+        [w_q, k] with strides (1, pitch) -- the strip's columns of B as rows, K
+        strided (the 2-D copy wrote k rows of `pitch` doubles)."""
+        s0, s1 = self.strips[j][q]
+        off = self.stage_off + j * self.slot_bytes
+        slot = buf[off: off + 8 * self.k * self.pitch]
+        return slot.view(torch.float64).view(self.k, self.pitch)[:, : s1 - s0].T
+

@@ -71,3 +71,34 @@ def test_split_signal_count_matches_kernel_grid():
     for rows, k in [(1, 1), (32, 128), (33, 129), (256, 16384), (255, 8192), (60, 700)]:
         res_ld = (k + 15) // 16 * 16
         assert lib.fpemu_split_mc_signals(rows, k) == -(-rows // 32) * -(-res_ld // 128)
+
+
+@pytest.mark.parametrize("world,k,n_mod,n,chunk", [(2, 70, 24, 600, 256), (3, 129, 24, 751, 512), (8, 33, 25, 300, 256)])
+def test_strip_views_read_back_what_the_copies_wrote(world, k, n_mod, n, chunk):
+    """Emulate the root's 2-D staging copy (k rows of the strip's width, row pitch
+    `pitch` doubles) on a CPU buffer and read it back through staging_strip; write
+    each strip's residues and exponents through chunk_views and check that every
+    chunk is tiled exactly by its strips."""
+    import torch
+
+    ld = _res_ld(k)
+    plan = plan_column_chunks(n, chunk)
+    L = NvlsLayout(world, k, n_mod, ld, plan)
+    buf = torch.zeros(L.cnt_off, dtype=torch.int8)  # the ring's buffer stops before the counters
+    B = torch.randn(k, n, dtype=torch.float64)
+    for j, (c0, c1) in enumerate(plan):
+        res, exps = L.chunk_views(buf, j)
+        assert res.shape == (n_mod, c1 - c0, ld) and exps.shape == (c1 - c0,)
+        for q, (s0, s1) in enumerate(L.strips[j]):
+            off = L.stage_off + j * L.slot_bytes
+            slot = buf[off: off + 8 * k * L.pitch].view(torch.float64).view(k, L.pitch)
+            slot[:, : s1 - s0] = B[:, c0 + s0: c0 + s1]          # the 2-D copy
+            X = L.staging_strip(buf, j, q)
+            assert X.shape == (s1 - s0, k) and (s1 == s0 or X.stride() == (1, L.pitch))
+            assert torch.equal(X, B[:, c0 + s0: c0 + s1].T)
+            res[:, s0:s1, :] = q + 1                             # the strip's split output
+            exps[s0:s1] = 1000 + q
+        owner = torch.tensor([q + 1 for q, (s0, s1) in enumerate(L.strips[j]) for _ in range(s1 - s0)],
+                             dtype=torch.int8)
+        assert torch.equal(res[0, :, 0], owner) and torch.equal(res[-1, :, -1], owner)
+        assert torch.equal(exps, owner.to(torch.int32) + 999)
