@@ -182,6 +182,37 @@ class _IpcChunks:
         overwritten by the next call once it has run."""
         self.gemm_done[c].record(stream)
 
+    def _drain(self):
+        torch.cuda.synchronize(self.device)
+
+    def _phases(self):
+        return ("A",)
+
+    def release(self, barrier):
+        """Free the buffer and the events.  Collective: every rank of the group
+        releases the same transport in the same call; `barrier()` meets them.
+        This device drains first; after the first meeting no rank has work on
+        any buffer of this transport, after the second no peer maps this one."""
+        R = self._rt
+        self._drain()
+        barrier()
+        for ptr in self._peer_ptr.values():
+            _check(R.cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle")
+        for evs in self._peer_ev.values():
+            for e in evs:
+                _check(R.cudaEventDestroy(e), "cudaEventDestroy")
+        self._peer_ptr, self._peer_ev = {}, {}
+        for i in (self.calls - 2, self.calls - 1):  # nobody waits on these any more
+            self._forget(i, self._phases())
+        barrier()
+        for evs in self.ev.values():
+            for e in evs:
+                _check(R.cudaEventDestroy(e), "cudaEventDestroy")
+        self.ev = {}
+        _check(R.cudaFree(self.ptr), "cudaFree")
+        self.ptr, self.buf = None, None
+        atexit.unregister(self.close)
+
     def close(self):
         for ptr in self._peer_ptr.values():
             try:
@@ -322,6 +353,9 @@ class CeRing(_IpcChunks):
 
     def _events_per_chunk(self, name):
         return self.world if name == "have" else 1
+
+    def _phases(self):
+        return self.phases
 
     def _have(self, owner, c, q):
         evs = self.ev["have"] if owner == self.rank else self.peer_events(owner, "have")

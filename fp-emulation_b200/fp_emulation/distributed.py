@@ -3,24 +3,25 @@
 The reference has no multi-GPU code; this is the build's one exchange step.
 A is split by row blocks: each rank holds its own rows, whose exponents are
 per row, so splitting them needs no communication, and C is sharded the same
-way.  B is needed whole everywhere: the root rank splits it into int8 residue
-planes plus column exponents and broadcasts them with NCCL over NVLink.  K is
-never split, so there is no reduction collective.
+way.  B, held by one root rank, is needed whole everywhere, as int8 residue
+planes plus column exponents.  K is never split, so there is no reduction
+collective.  One process per GPU (torch.distributed).
 
-The broadcast is pipelined by column chunks of B.  The root splits chunk c
-and posts its broadcast on NCCL's stream; every rank runs the fused GEMM + CRT
-for chunk c (its rows x the chunk's columns of C) as soon as chunk c has
-arrived, while chunk c+1 is in flight.  The GEMM leaves a few SMs free so
-NCCL's kernels can run next to it.  One process per GPU (torch.distributed,
-backend "nccl").
+The product is pipelined by column chunks of B: every rank runs the fused GEMM
++ CRT for chunk c (its rows x the chunk's columns of C) as soon as chunk c's
+residues are in its memory, while later chunks are in flight.  How they get
+there is the transport (TRANSPORT below): a copy-engine chain through CUDA IPC
+(default), a copy-engine ring of per-rank strips, NVLink multicast stores, or
+NCCL broadcasts.
 
-The orchestration is written against a small backend (`_GpuOps`) so that the
-same pipeline can be exercised with CPU ranks over gloo in tests.
+The NCCL pipeline is written against a small backend (`_GpuOps`) so that it
+can be exercised with CPU ranks over gloo in tests.
 """
 from __future__ import annotations
 
 import os
 import warnings
+from collections import OrderedDict
 from dataclasses import dataclass
 
 import torch
@@ -168,7 +169,33 @@ def rowsharded_product(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, c
     return C
 
 
-_TRANSPORTS = {}
+# Transports hold large device buffers (B's residues for every chunk of one
+# column layout), so each process group keeps at most MAX_TRANSPORTS of them,
+# the least recently used evicted first.  The products are collective calls made
+# in the same order on every rank, so every rank evicts the same transport in the
+# same call, and the release can meet the group.
+MAX_TRANSPORTS = int(os.environ.get("FPEMU_MAX_TRANSPORTS", "4"))
+_TRANSPORTS = {}  # id(group) -> OrderedDict(key -> transport), oldest first
+
+
+def _group_barrier(group, device):
+    if device is not None and dist.get_backend(group) == "nccl":
+        dist.barrier(group=group, device_ids=[device.index])
+    else:
+        dist.barrier(group=group)
+
+
+def _cached_transport(group, key, make):
+    """The transport for `key` (made by `make()` on a miss), most recent first."""
+    cache = _TRANSPORTS.setdefault(id(group), OrderedDict())
+    tr = cache.pop(key, None)
+    if tr is None:
+        while cache and len(cache) >= max(1, MAX_TRANSPORTS):
+            _, old = cache.popitem(last=False)
+            old.release(lambda: _group_barrier(group, getattr(old, "device", None)))
+        tr = make()
+    cache[key] = tr
+    return tr
 
 
 def _align256(x):
@@ -181,15 +208,15 @@ def rowsharded_product_nvls(A_local, B, n, k, bits, n_mod, ops, root=0, group=No
 
     dev = A_local.device
     plan = plan_column_chunks(n, chunk_cols)
-    key = ("nvls", id(group), root, dev.index, k, n, n_mod, tuple(plan))
-    tr = _TRANSPORTS.get(key)
-    if tr is None:
+    key = ("nvls", root, dev.index, k, n, n_mod, tuple(plan))
+
+    def make():
         try:
-            tr = NvlsTransport(group, root, dev, k, n, n_mod, _res_ld(k), plan)
+            return NvlsTransport(group, root, dev, k, n, n_mod, _res_ld(k), plan)
         except RuntimeError as exc:  # no multicast mapping for this group or size
             raise _NvlsSetupError(str(exc)) from exc
-        _TRANSPORTS[key] = tr
-    return tr.product(A_local, B, ops, bits)
+
+    return _cached_transport(group, key, make).product(A_local, B, ops, bits)
 
 
 class _NvlsSetupError(RuntimeError):
@@ -209,10 +236,9 @@ def rowsharded_product_ring(A_local, B, n, k, bits, n_mod, ops, root=0, group=No
     m = A_local.shape[0]
     ld = _res_ld(k)
     plan = plan_column_chunks(n, chunk_cols)
-    key = ("ce-ring", id(group), root, dev.index, k, n, n_mod, tuple(plan))
-    tr = _TRANSPORTS.get(key)
-    if tr is None:
-        tr = _TRANSPORTS[key] = CeRing(group, root, dev, StripLayout(dist.get_world_size(group), k, n_mod, ld, plan))
+    key = ("ce-ring", root, dev.index, k, n, n_mod, tuple(plan))
+    tr = _cached_transport(group, key, lambda: CeRing(group, root, dev,
+                                                      StripLayout(dist.get_world_size(group), k, n_mod, ld, plan)))
     L = tr.layout
     stream = torch.cuda.current_stream(dev)
 
@@ -300,10 +326,8 @@ def rowsharded_product_ce(A_local, B, n, k, bits, n_mod, ops, root=0, group=None
     wmax = max(c1 - c0 for c0, c1 in plan)
     res_bytes = _align256(n_mod * wmax * ld)
     chunk_bytes = res_bytes + _align256(wmax * 4)
-    key = (kind, id(group), root, dev.index, chunk_bytes, len(plan))
-    tr = _TRANSPORTS.get(key)
-    if tr is None:
-        tr = _TRANSPORTS[key] = TRANSPORTS[kind](group, root, dev, chunk_bytes, len(plan))
+    key = (kind, root, dev.index, chunk_bytes, len(plan))
+    tr = _cached_transport(group, key, lambda: TRANSPORTS[kind](group, root, dev, chunk_bytes, len(plan)))
     stream = torch.cuda.current_stream(dev)
     views = []
     for c, (c0, c1) in enumerate(plan):

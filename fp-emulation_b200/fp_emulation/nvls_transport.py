@@ -204,3 +204,12 @@ class NvlsTransport:
             torch.cuda.synchronize(self.device)
         except Exception:
             pass
+
+    def release(self, barrier):
+        """Drop the symmetric buffer.  Collective (every rank releases the same
+        transport in the same call): this device drains, the group meets -- after
+        which no rank stores into another's copy -- then the references go."""
+        torch.cuda.synchronize(self.device)
+        barrier()
+        self.buf = self.handle = self.colmax = None
+        atexit.unregister(self.close)

@@ -59,6 +59,7 @@ class FakeRt:
         self.copies = 0
         self.copies2d = 0
         self.label = ""
+        self.closed = self.destroyed = self.freed = 0
 
     def _rec_key(self, ev):
         return f"fake_rec/{ev[0]}/{ev[1]}"
@@ -84,6 +85,15 @@ class FakeRt:
         return OK, (int(owner), int(idx))
 
     def cudaIpcCloseMemHandle(self, ptr):
+        self.closed += 1
+        return (OK,)
+
+    def cudaEventDestroy(self, ev):
+        self.destroyed += 1
+        return (OK,)
+
+    def cudaFree(self, ptr):
+        self.freed += 1
         return (OK,)
 
     def cudaEventRecord(self, ev, stream):
@@ -315,3 +325,98 @@ def test_ring_waits_bind_to_the_right_records(world, root):
         assert copies2d == (W * nc * calls if rank == root else 0) + (W - 1) * nc * calls
         assert copies == (W - 1) * nc * calls
         assert left == [calls - 2, calls - 1], left
+
+
+# -- the bounded transport cache: collective least-recently-used eviction --------
+
+def _cache_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        from fp_emulation import ce_transport as ct
+        from fp_emulation import distributed as D
+
+        D.MAX_TRANSPORTS = 2
+        store = dist.distributed_c10d._get_default_store()
+        fake = FakeRt(rank, store)
+
+        class FakeChain(ct.CeChain):
+            _rt = fake
+
+            def _device_ctx(self):
+                return contextlib.nullcontext()
+
+            def _wrap_buffer(self, ptr, nbytes):
+                return None
+
+            def _local_event(self):
+                return _LocalEvent()
+
+            def _new_stream(self):
+                return _Stream()
+
+            def _current_stream(self):
+                return _Stream()
+
+            def _drain(self):
+                pass
+
+        made = {}
+
+        def make(tag):
+            def f():
+                made[tag] = FakeChain(None, 0, None, chunk_bytes=4096, n_chunks=2, pieces=2)
+                return made[tag]
+            return f
+
+        main = _Stream()
+        for tag in ["a", "b", "a", "c", "d"]:  # a, b; a again (b is now the oldest); c evicts b; d evicts a
+            ch = D._cached_transport(None, tag, make(tag))
+            fake.chain = ch
+            if rank == 0:
+                ch.root_begin(main)
+                for c in range(2):
+                    ch.root_before_write(c)
+                    ch.root_after_write(c)
+                ch.root_end()
+            else:
+                ch.pull()
+            for c in range(2):
+                ch.wait_chunk(c, main)
+                ch.after_gemm(c, main)
+        dist.barrier()
+        released = sorted(t for t, ch in made.items() if ch.ptr is None)
+        live = list(D._TRANSPORTS[id(None)].keys())
+        keys_left = [t for t in released for i in range(2) if store.check([made[t]._key(rank, i, "A")])]
+        q.put((rank, "ok", (released, live, fake.freed, fake.destroyed, fake.closed, keys_left)))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, "error", traceback.format_exc()))
+
+
+def test_transport_cache_evicts_the_same_transport_on_every_rank():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_cache_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict((r, (st, pl)) for r, st, pl in (q.get(timeout=180) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=60)
+    for rank, (status, payload) in results.items():
+        assert status == "ok", payload
+        released, live, freed, destroyed, closed, keys_left = payload
+        assert released == ["a", "b"] and live == ["c", "d"]
+        assert freed == 2 and keys_left == []
+        # Own events: 2 chunks x 2 pieces per transport.  Rank 1 also opened its
+        # predecessor's buffer and events in every call; the root opened its
+        # successor's events in a's second call only (WAR waits start at call 1).
+        if rank == 0:
+            assert (destroyed, closed) == (4 + 4 + 4, 0)
+        else:
+            assert (destroyed, closed) == (2 * (4 + 4), 2)
