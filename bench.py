@@ -469,7 +469,9 @@ def run_ours(args):
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
                          "peak_burst": round(peak_burst, 1), "frac_burst": round(achieved / peak_burst, 4),
                          "ops_per_launch": int8_ops, "launch_ms": round(gemm_ms, 3),
-                         "traffic": gemm_traffic_per_launch(n) if args.config == 2 else None},
+                         # measured for the single-GPU launch at n = 16384 (profiles/); the
+                         # multi-GPU launches are per column chunk, with no capture of their own
+                         "traffic": gemm_traffic_per_launch(n) if args.config == 2 and world == 1 else None},
             "int8_tc_util": round(achieved / peak_burst, 4),
             "stages_ms": stages,
             "gpu_launches": launches,
