@@ -106,12 +106,7 @@ class NvlsTransport:
         return base + self.layout.counter(kind, j)
 
     def chunk_views(self, j):
-        c0, c1 = self.plan[j]
-        w = c1 - c0
-        blk = self.buf[j * self.chunk_bytes:(j + 1) * self.chunk_bytes]
-        res = blk[: self.n_mod * w * self.ld].view(self.n_mod, w, self.ld)
-        exps = blk[self.res_bytes: self.res_bytes + 4 * w].view(torch.int32)
-        return res, exps
+        return self.layout.chunk_views(self.buf, j)
 
     # -- enqueue helpers ------------------------------------------------------
     def _wait(self, addrs, target, where, stream):
