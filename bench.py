@@ -248,14 +248,17 @@ def run_ours(args):
         n_chunks = len(fdist.plan_column_chunks(n))
         product = fdist.rowsharded_product_auto
 
+    last_step = {}
+
     def step_dist(record):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)] if record else None
         dist_ops.timing = gemm_timing if record else None
+        first = len(gemm_timing)
         if ev: ev[0].record(stream)
-        product(A, B, n, k, bits, n_mod, dist_ops, root=root)
+        last_step["C"] = product(A, B, n, k, bits, n_mod, dist_ops, root=root)
         if ev:
             ev[1].record(stream)
-            n_steps_events.append(ev)
+            n_steps_events.append(ev + [first, len(gemm_timing)])
 
     def step(record):
         if world > 1:
@@ -322,11 +325,10 @@ def run_ours(args):
     if code[0]:
         raise RuntimeError(f"device-side failure in the timed region: {code}")
     ms_step = elapsed_ms / args.steps
+    parity = parity_gate(torch, dist, A, B, last_step.pop("C") if world > 1 else C, n, k, world, rank, root, dev)
     transport_used = None
     if world > 1:
         transport_used = fdist.TRANSPORT if fdist.BCAST_MODE == "residues" else "nccl"
-        if transport_used == "nvls" and not fdist._NVLS_OK.get(id(None), False):
-            transport_used = "ce"
     flops = 2.0 * M * n * k
     value = flops / (ms_step * 1e-3) / 1e12
 
@@ -340,8 +342,20 @@ def run_ours(args):
         # Per chunk GEMM launches of the pipelined row-sharded product (this rank).
         gemm_ms = statistics.mean(s_.elapsed_time(e_) for s_, e_, _ in gemm_timing)
         int8_ops = statistics.mean(o for _, _, o in gemm_timing)
-        stages = {"gemm_crt_per_chunk": round(gemm_ms, 3), "chunks": n_chunks,
-                  "step_rank0": round(statistics.mean(e[0].elapsed_time(e[1]) for e in n_steps_events), 3)}
+        # Where each rank's step goes: before its first chunk GEMM (A's split and the
+        # first chunk's transfer), GEMMs, waits between GEMMs, and after the last.
+        br = {"fill": [], "gemm": [], "gaps": [], "tail": []}
+        for e0, e1, i0, i1 in n_steps_events:
+            g = gemm_timing[i0:i1]
+            br["fill"].append(e0.elapsed_time(g[0][0]))
+            br["gemm"].append(sum(a.elapsed_time(b) for a, b, _ in g))
+            br["gaps"].append(sum(g[j - 1][1].elapsed_time(g[j][0]) for j in range(1, len(g))))
+            br["tail"].append(g[-1][1].elapsed_time(e1))
+        mine = {key: round(statistics.mean(v), 3) for key, v in br.items()}
+        mine["step"] = round(statistics.mean(e0.elapsed_time(e1) for e0, e1, _, _ in n_steps_events), 3)
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, mine)
+        stages = {"gemm_crt_per_chunk": round(gemm_ms, 3), "chunks": n_chunks, "per_rank": per_rank}
     achieved = int8_ops / (gemm_ms * 1e-3) / 1e12
     peaks = measured_peaks()
     # MEASURED_PEAKS.json has no INT8 figure; B200's dense INT8 rate is twice its dense
@@ -355,20 +369,14 @@ def run_ours(args):
     else:
         peak, peak_src = 2.0 * 1400.0, "2 x 1.4 PFLOP/s sustained bf16 of fallback"
         peak_burst = 2.0 * 1590.0
-    # Our kernels per step: split A (1), split B on the root (column max + split: 2 per
-    # chunk), one GEMM per chunk (1 chunk on a single GPU).
     # Our kernels per step and rank.  One GPU: split A, split B (column max +
     # split), the fused GEMM.  Root-split transports (ce, nccl): split A, split B
-    # per chunk on the root (2 kernels), one GEMM per chunk.  NVLS: split A, and
-    # per chunk two counter waits + the strip's 2 split kernels on the split
-    # stream, a wait + the GEMM + a signal on the GEMM stream, and on the root a
-    # wait + a signal beside its staging copies.
+    # per chunk on the root (2 kernels), one GEMM per chunk.  Ring: split A, and per
+    # chunk the strip's 2 split kernels and one GEMM.
     if world == 1:
         per_rank = 4
     elif transport_used == "ce-ring":
         per_rank = 1 + 3 * n_chunks
-    elif transport_used == "nvls":
-        per_rank = 1 + 7 * n_chunks + (2 * n_chunks if rank == root else 0)
     else:
         per_rank = 1 + n_chunks + (2 * n_chunks if rank == root else 0)
     launches = int(sum_over_ranks(per_rank * args.steps))
@@ -474,6 +482,7 @@ def run_ours(args):
                          "traffic": gemm_traffic_per_launch(n) if args.config == 2 and world == 1 else None},
             "int8_tc_util": round(achieved / peak_burst, 4),
             "stages_ms": stages,
+            "parity": parity,
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }
@@ -482,6 +491,44 @@ def run_ours(args):
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+def parity_gate(torch, dist, A_local, B_root, C_local, n, k, world, rank, root, dev):
+    """Checker, after the timed region: every rank compares a sampled block of
+    its rows of the last step's C -- its first, last and two interior rows, by
+    64 columns that include the first and the last -- bit for bit with the CPU
+    oracle's product of the same rows of A and columns of B (row and column
+    exponents span all of K, so the block of the product is exact).  B's
+    sampled columns come from the root.  Any mismatch on any rank raises on
+    every rank."""
+    import numpy as np
+
+    from oracle import ozaki_oracle as oo
+
+    m = C_local.shape[0]
+    rows = sorted({0, m // 3, (2 * m) // 3, m - 1}) if m else []
+    cols = sorted(set(np.linspace(0, n - 1, min(n, 64)).round().astype(int).tolist()))
+    cols_t = torch.tensor(cols, device=dev)
+    if rank == root:
+        Bc = B_root.index_select(1, cols_t).contiguous()
+    else:
+        Bc = torch.empty((k, len(cols)), dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.broadcast(Bc, src=root)
+    ok = True
+    if rows:
+        rows_t = torch.tensor(rows, device=dev)
+        got = C_local.index_select(0, rows_t).index_select(1, cols_t).cpu().numpy()
+        want = oo.ozaki2_matmul(A_local.index_select(0, rows_t).cpu().numpy(), Bc.cpu().numpy())
+        ok = bool(np.array_equal(got.view(np.int64), want.view(np.int64)))
+    bad = torch.tensor([0 if ok else 1], dtype=torch.int32, device=dev)
+    if world > 1:
+        dist.all_reduce(bad, op=dist.ReduceOp.SUM)
+    if bad.item():
+        raise RuntimeError(f"parity gate: {bad.item()} rank(s) differ from the oracle on the sampled block")
+    return {"status": "bit-exact", "checker": "CPU oracle (oracle/ozaki_oracle.py), after the timed region",
+            "sampled": {"ranks": world, "rows_per_rank": len(rows), "cols": len(cols),
+                        "rows_rank0": rows if rank == 0 else None, "cols_first_last": [cols[0], cols[-1]]}}
 
 
 def side_numbers(torch, dev, A, B, b_res, m, n, k, n_mod, rank, root, world, args):

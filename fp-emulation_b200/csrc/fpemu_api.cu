@@ -84,6 +84,15 @@ int device_info(DevInfo* out) {
     return FPEMU_OK;
 }
 
+// Test hook of the failure-detection tests (FPEMU_TEST_STALL_UNIT=i): the TMA
+// producers of the GEMM's first unit stop delivering at their unit i, so the
+// consumers' bounded waits run out exactly as they would behind a stalled
+// producer.  Read on every call; -1 (unset) disables it.
+int test_stall_idx() {
+    const char* s = getenv("FPEMU_TEST_STALL_UNIT");
+    return s && *s ? atoi(s) : -1;
+}
+
 uint64_t wait_budget_ns() {
     static uint64_t v = [] {
         const char* s = getenv("FPEMU_WAIT_BUDGET_MS");
@@ -279,10 +288,6 @@ int gemm_units(const DevInfo& d, int64_t m, int64_t n) {
     return (int)((tiles + waves - 1) / waves);
 }
 
-int gemm_ctas(const DevInfo& d, int64_t m, int64_t n) {
-    return use_pairs() ? 2 * gemm_units<MainCfg>(d, m, n) : gemm_units<SingleCfg>(d, m, n);
-}
-
 // Tile rows per raster band (FPEMU_BAND_ROWS).  Default 8: with 256-row tiles and
 // K = 16384 a band's A strips for one modulus are 32 MB, which stays resident in
 // the L2 while the band's columns stream past; measured on B200 at n = 16384 the
@@ -380,7 +385,7 @@ int launch_split(const SplitParams& P, uint64_t* colmax, const DevInfo& d, cudaS
         SplitParams Q = P;
         Q.colmax = colmax;
         dim3 g2((unsigned)((P.rows + kTileR - 1) / kTileR), (unsigned)((P.res_ld + kTileK - 1) / kTileK));
-        split_strided_kernel<false><<<g2, 256, 0, st>>>(Q);
+        split_strided_kernel<<<g2, 256, 0, st>>>(Q);
     }
     FPEMU_CUDA(cudaGetLastError());
     return FPEMU_OK;
@@ -400,6 +405,10 @@ int launch_gemm_cfg(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int
     P.num_tiles = P.tiles_m * P.tiles_n;
     P.band_rows = band_rows();
     P.budget_ns = wait_budget_ns();
+    // A producer normally waits at a pass boundary for at most about one tile's
+    // K loop (tens of microseconds at k = 16384); past this it stops aligning.
+    P.align_budget_ns = std::min<uint64_t>(P.budget_ns, 1000000ull + 20ull * (uint64_t)P.k);
+    P.test_stall_idx = test_stall_idx();
     mod_consts(P.n_mod, &P.mc);
     int units = gemm_units<Cfg>(d, m, n);
     if (max_ctas > 0 && units > max_ctas / Cfg::CG) units = max_ctas / Cfg::CG;
@@ -461,6 +470,38 @@ int noalloc_scratch(uint8_t** out) {
         addr[dev] = static_cast<uint8_t*>(p);
     }
     *out = addr[dev];
+    return FPEMU_OK;
+}
+
+// Host-visible mirrors of g_device_error, one per device: a pinned host block
+// mapped into the device address space, its device address stored in
+// g_host_error of that device.  Set up by fpemu_watch_errors (which allocates
+// pinned host memory once per process; no device memory).
+int host_error_slot(volatile DeviceError** out, bool create) {
+    static std::mutex mu;
+    static DeviceError* block = nullptr;
+    static bool armed[64] = {};
+    int dev = 0;
+    FPEMU_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(FPEMU_ERR_NO_DEVICE, "device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lk(mu);
+    if (!armed[dev]) {
+        if (!create) {
+            *out = nullptr;
+            return FPEMU_OK;
+        }
+        if (block == nullptr) {
+            void* p = nullptr;
+            FPEMU_CUDA(cudaHostAlloc(&p, 64 * sizeof(DeviceError), cudaHostAllocMapped | cudaHostAllocPortable));
+            memset(p, 0, 64 * sizeof(DeviceError));
+            block = static_cast<DeviceError*>(p);
+        }
+        DeviceError* dptr = nullptr;
+        FPEMU_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&dptr), block + dev, 0));
+        FPEMU_CUDA(cudaMemcpyToSymbol(g_host_error, &dptr, sizeof dptr));
+        armed[dev] = true;
+    }
+    *out = block + dev;
     return FPEMU_OK;
 }
 
@@ -573,108 +614,6 @@ int fpemu_split(int64_t rows, int64_t k, const double* X, int64_t s_row, int64_t
     P.n_mod = n_mod;
     mod_consts(n_mod, &P.mc);
     return launch_split(P, colmax_scratch, d, static_cast<cudaStream_t>(stream));
-}
-
-// ------------------------------------------- multi-GPU (NVLS) primitives --
-
-// The kernels below run beside the persistent GEMM, and the waits may spin for a
-// while.  An SM's shared-memory carveout is fixed while blocks are resident, so a
-// small-carveout SM held by one of them could not host a GEMM CTA (which needs
-// ~193 KB); ask for the largest shared-memory carveout so they leave the SM in
-// a configuration the GEMM fits.  A scheduling preference, set once per device.
-static void prefer_max_shared_carveout() {
-    static std::mutex mu;
-    static bool done[64] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
-    std::lock_guard<std::mutex> lk(mu);
-    if (done[dev]) return;
-    const int carve = cudaSharedmemCarveoutMaxShared;
-    cudaFuncSetAttribute(wait_counters_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, carve);
-    cudaFuncSetAttribute(signal_counter_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, carve);
-    cudaFuncSetAttribute(split_strided_kernel<true>, cudaFuncAttributePreferredSharedMemoryCarveout, carve);
-    cudaGetLastError();  // a refused hint is not an error of the call
-    done[dev] = true;
-}
-
-int64_t fpemu_split_mc_signals(int64_t rows, int64_t k) {
-    if (rows <= 0 || k < 1) return 0;
-    const int64_t res_ld = res_ld_for(k);
-    return ((rows + kTileR - 1) / kTileR) * ((res_ld + kTileK - 1) / kTileK);
-}
-
-int fpemu_split_mc(int64_t rows, int64_t k, const double* X, int64_t s_row, int64_t s_k, int bits, int n_mod,
-                   int8_t* res_mc, int64_t res_ld, int64_t res_plane, int32_t* exps_mc, uint64_t* colmax_scratch,
-                   uint64_t* done_mc, void* stream) {
-    DevInfo d;
-    FPEMU_TRY(device_info(&d));
-    FPEMU_TRY(bits_ok(bits));
-    if (rows < 0 || k < 1 || s_row < 0 || s_k < 0) return fail(FPEMU_ERR_INVALID, "split_mc: bad sizes or strides");
-    if (s_k == 1) return fail(FPEMU_ERR_UNSUPPORTED, "split_mc: only strided K (s_k != 1) is supported");
-    if (n_mod < 1 || n_mod > kMaxModuli) return fail(FPEMU_ERR_UNSUPPORTED, "n_mod=%d outside [1, %d]", n_mod, kMaxModuli);
-    if (res_ld != res_ld_for(k) || res_plane < rows * res_ld || res_plane % 16 != 0)
-        return fail(FPEMU_ERR_INVALID, "split_mc: res_ld must be %lld and res_plane >= rows*res_ld, a multiple of 16",
-                    (long long)res_ld_for(k));
-    if (rows == 0) return FPEMU_OK;
-    if (!X || !res_mc || !exps_mc || !colmax_scratch || !done_mc) return fail(FPEMU_ERR_INVALID, "split_mc: null pointer");
-    if (reinterpret_cast<uintptr_t>(res_mc) % 16 != 0 || reinterpret_cast<uintptr_t>(exps_mc) % 4 != 0 ||
-        reinterpret_cast<uintptr_t>(done_mc) % 8 != 0)
-        return fail(FPEMU_ERR_INVALID, "split_mc: misaligned res (16), exps (4) or counter (8)");
-    SplitParams P;
-    memset(&P, 0, sizeof P);
-    P.X = X;
-    P.rows = rows;
-    P.k = k;
-    P.s_row = s_row;
-    P.s_k = s_k;
-    P.res = res_mc;
-    P.res_ld = res_ld;
-    P.res_plane = res_plane;
-    P.exps = exps_mc;
-    P.bits = bits;
-    P.n_mod = n_mod;
-    P.colmax = colmax_scratch;
-    P.done = reinterpret_cast<unsigned long long*>(done_mc);
-    mod_consts(n_mod, &P.mc);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    FPEMU_CUDA(cudaMemsetAsync(colmax_scratch, 0, (size_t)rows * 8, st));
-    dim3 g1((unsigned)((rows + 255) / 256), (unsigned)((k + kColmaxK - 1) / kColmaxK));
-    split_colmax_kernel<<<g1, 256, 0, st>>>(P, reinterpret_cast<unsigned long long*>(colmax_scratch));
-    FPEMU_CUDA(cudaGetLastError());
-    dim3 g2((unsigned)((rows + kTileR - 1) / kTileR), (unsigned)((res_ld + kTileK - 1) / kTileK));
-    prefer_max_shared_carveout();
-    split_strided_kernel<true><<<g2, 256, 0, st>>>(P);
-    FPEMU_CUDA(cudaGetLastError());
-    return FPEMU_OK;
-}
-
-int fpemu_wait_counters(const uint64_t* const* counters, int n, uint64_t target, int where, void* stream) {
-    if (n < 0 || n > kMaxWaitCounters) return fail(FPEMU_ERR_INVALID, "wait_counters: n=%d outside [0, %d]", n, kMaxWaitCounters);
-    if (n == 0) return FPEMU_OK;
-    if (!counters) return fail(FPEMU_ERR_INVALID, "wait_counters: null list");
-    CounterList L;
-    memset(&L, 0, sizeof L);
-    for (int i = 0; i < n; ++i) {
-        if (!counters[i] || reinterpret_cast<uintptr_t>(counters[i]) % 8 != 0)
-            return fail(FPEMU_ERR_INVALID, "wait_counters: counter %d null or misaligned", i);
-        L.p[i] = reinterpret_cast<const unsigned long long*>(counters[i]);
-    }
-    L.n = n;
-    prefer_max_shared_carveout();
-    wait_counters_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(L, (unsigned long long)target,
-                                                                         (int64_t)wait_budget_ns(), where);
-    FPEMU_CUDA(cudaGetLastError());
-    return FPEMU_OK;
-}
-
-int fpemu_signal_counter(uint64_t* counter, int multicast, void* stream) {
-    if (!counter || reinterpret_cast<uintptr_t>(counter) % 8 != 0)
-        return fail(FPEMU_ERR_INVALID, "signal_counter: null or misaligned counter");
-    prefer_max_shared_carveout();
-    signal_counter_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-        reinterpret_cast<unsigned long long*>(counter), multicast ? 1 : 0);
-    FPEMU_CUDA(cudaGetLastError());
-    return FPEMU_OK;
 }
 
 int fpemu_gemm_residues(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_res, const int8_t* b_res,
@@ -863,7 +802,27 @@ int fpemu_device_error(int* code, int* where, int* block, int* detail, int clear
         DeviceError z;
         memset(&z, 0, sizeof z);
         FPEMU_CUDA(cudaMemcpyToSymbol(g_device_error, &z, sizeof z));
+        volatile DeviceError* h = nullptr;
+        FPEMU_TRY(host_error_slot(&h, false));
+        if (h != nullptr) h->code = 0;
     }
+    return FPEMU_OK;
+}
+
+int fpemu_watch_errors(void) {
+    volatile DeviceError* h = nullptr;
+    return host_error_slot(&h, true);
+}
+
+int fpemu_poll_error(int* code, int* where, int* block, int* detail) {
+    if (code == nullptr) return fail(FPEMU_ERR_INVALID, "code is null");
+    volatile DeviceError* h = nullptr;
+    FPEMU_TRY(host_error_slot(&h, false));
+    if (h == nullptr) return fail(FPEMU_ERR_INVALID, "fpemu_poll_error: fpemu_watch_errors was not called on this device");
+    *code = h->code;
+    if (where) *where = h->where;
+    if (block) *block = h->block;
+    if (detail) *detail = h->detail;
     return FPEMU_OK;
 }
 

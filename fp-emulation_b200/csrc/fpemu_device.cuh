@@ -30,13 +30,16 @@ enum : int {
     kWaitTmemEmpty = 4,  // MMA warp waiting for the epilogue to drain TMEM
     kWaitDrainTma = 5,   // producer draining its loads at exit
     kWaitDrainMma = 6,   // MMA warp draining its MMAs at exit
-    kWaitPass = 7,       // producer waiting for every CTA to finish issuing a modulus pass
-    kWaitCounter = 8,    // a stream-ordered wait on another GPU's progress counter
 };
 
 // The first device-side failure on this device (one copy per device that loads
 // the library); read and cleared by fpemu_device_error().
 __device__ DeviceError g_device_error;
+
+// Optional host-visible copy of the first failure: a pinned, mapped host
+// DeviceError set up by fpemu_watch_errors() for this device (null until then).
+// The host reads it without synchronising (fpemu_poll_error).
+__device__ DeviceError* g_host_error;
 
 __device__ __forceinline__ void report_error(DeviceError* err, int code, int where, int detail) {
     if (err != nullptr && atomicCAS(&err->code, 0, code) == 0) {
@@ -44,6 +47,15 @@ __device__ __forceinline__ void report_error(DeviceError* err, int code, int whe
         err->block = (int)blockIdx.x;
         err->detail = detail;
         __threadfence();
+        volatile DeviceError* h = g_host_error;
+        if (h != nullptr) {
+            h->where = where;
+            h->block = (int)blockIdx.x;
+            h->detail = detail;
+            __threadfence_system();
+            h->code = code;  // last: a non-zero code means the other fields are set
+            __threadfence_system();
+        }
     }
 }
 

@@ -41,7 +41,6 @@ struct SplitParams {
     int64_t res_ld, res_plane;
     int32_t* exps;
     const uint64_t* colmax;  // strided variant only
-    unsigned long long* done;  // multicast variant only: per-CTA completion counter
     int bits, n_mod;
     ModConsts mc;
 };
@@ -57,6 +56,10 @@ enum GemmMode : int { kModeRaw = 0, kModeResidue = 1, kModeCrt = 2 };
 //     slot per CTA (bounded workspace), at the cost of re-reading A and B strips
 //     from DRAM for every modulus.
 enum GemmSched : int { kSchedModulusMajor = 0, kSchedTileMajor = 1 };
+
+// Index of the "stop aligning" flag in the 64 pass counters of the modulus-major
+// schedule (passes use [0, n_mod), n_mod <= 25).
+constexpr int kPassGiveUp = 63;
 
 struct GemmParams {
     int m, n, k, n_mod;
@@ -75,8 +78,11 @@ struct GemmParams {
     int64_t scratch_slot;  // bytes of one staging slot (one CTA's share of one tile)
     int sched;             // GemmSched
     int tail;              // modulus-major: interleave the last two passes (CRT next to light epilogues)
-    unsigned int* pass_ctr;  // modulus-major: n_mod zeroed counters aligning the producers per pass
+    unsigned int* pass_ctr;  // modulus-major: zeroed counters aligning the producers per pass
+                             // ([l] for pass l; [kPassGiveUp] set when alignment is abandoned)
     uint64_t budget_ns;    // bound on every mbarrier wait
+    uint64_t align_budget_ns;  // how long a producer waits at a pass boundary before it stops aligning
+    int test_stall_idx;    // test hook (-1 = off): unit 0's producers issue nothing from this unit on
     ModConsts mc;
     CrtConsts cc;
 };

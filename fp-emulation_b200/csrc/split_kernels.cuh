@@ -14,7 +14,7 @@
 //                        transposes through shared memory.
 #pragma once
 
-#include "nvls.cuh"
+#include "fpemu_device.cuh"
 
 namespace fpemu {
 
@@ -92,32 +92,29 @@ __device__ __forceinline__ uint32_t prime_rem(uint32_t y) {
     return y - (__umulhi(y, magic) >> shift) * p;
 }
 
-// MC: `dst` is an NVLink multicast address and the vector goes to every GPU
-// of the group (multimem.st); otherwise an ordinary 16-byte store.
-template <int L, bool MC>
+template <int L>
 __device__ __forceinline__ void store_plane(const uint32_t (&y)[16], int8_t* dst, int64_t res_plane) {
     uint32_t w[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q)
         w[q] = prime_rem<L>(y[4 * q]) | (prime_rem<L>(y[4 * q + 1]) << 8) | (prime_rem<L>(y[4 * q + 2]) << 16) |
                (prime_rem<L>(y[4 * q + 3]) << 24);
-    if constexpr (MC) mc_store_16(dst + (int64_t)L * res_plane, make_uint4(w[0], w[1], w[2], w[3]));
-    else *reinterpret_cast<uint4*>(dst + (int64_t)L * res_plane) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(dst + (int64_t)L * res_plane) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-template <int G, int L, bool MC>
+template <int G, int L>
 __device__ __forceinline__ void store_group_planes(const uint32_t (&y)[16], int n_mod, int8_t* dst,
                                                    int64_t res_plane) {
     constexpr int end = kGroupFirst[G + 1];
     if constexpr (L < end) {
         if (L < n_mod) {
-            store_plane<L, MC>(y, dst, res_plane);
-            store_group_planes<G, L + 1, MC>(y, n_mod, dst, res_plane);
+            store_plane<L>(y, dst, res_plane);
+            store_group_planes<G, L + 1>(y, n_mod, dst, res_plane);
         }
     }
 }
 
-template <int G, bool MC>
+template <int G>
 __device__ __forceinline__ void store_groups_from(const double (&x)[16], int n_mod, int8_t* dst,
                                                   int64_t res_plane) {
     if constexpr (G < kNumGroups) {
@@ -126,8 +123,8 @@ __device__ __forceinline__ void store_groups_from(const double (&x)[16], int n_m
             uint32_t y[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) y[j] = group_rem<G>(x[j]);
-            store_group_planes<G, first, MC>(y, n_mod, dst, res_plane);
-            store_groups_from<G + 1, MC>(x, n_mod, dst, res_plane);
+            store_group_planes<G, first>(y, n_mod, dst, res_plane);
+            store_groups_from<G + 1>(x, n_mod, dst, res_plane);
         }
     }
 }
@@ -135,10 +132,9 @@ __device__ __forceinline__ void store_groups_from(const double (&x)[16], int n_m
 // Residues of 16 consecutive scaled elements for every modulus, stored as one
 // 16-byte vector per plane.  `dst` is plane 0 of the chunk; planes are
 // res_plane apart.
-template <bool MC = false>
 __device__ __forceinline__ void store_chunk_residues(const double (&x)[16], int n_mod, int8_t* dst,
                                                      int64_t res_plane) {
-    store_groups_from<0, MC>(x, n_mod, dst, res_plane);
+    store_groups_from<0>(x, n_mod, dst, res_plane);
 }
 
 // ---------------------------------------------------------------------------
@@ -254,11 +250,6 @@ __global__ void __launch_bounds__(256) split_colmax_kernel(const __grid_constant
 constexpr int kTileR = 32;
 constexpr int kTileK = 128;
 
-// MC: P.res and P.exps are NVLink multicast addresses (every GPU of the group
-// receives the residues), and each CTA adds 1 to the multicast counter P.done
-// with release semantics once its stores are issued, so a GPU whose counter
-// has reached the number of CTAs of every producer holds the whole chunk.
-template <bool MC>
 __global__ void __launch_bounds__(256) split_strided_kernel(const __grid_constant__ SplitParams P) {
     // Element (t, r) sits at tile[t][r ^ swz(t)], swz(t) = 4 * ((t / 16) % 8), so the
     // compute phase (8 k-chunks x 4 rows per warp) hits every bank pair once per
@@ -289,10 +280,7 @@ __global__ void __launch_bounds__(256) split_strided_kernel(const __grid_constan
     const int64_t t0 = k0 + 16 * kc;
     if (row < P.rows && t0 < P.res_ld) {
         const int e = exp_from_maxbits(P.colmax[row]);
-        if (blockIdx.y == 0 && kc == 0) {
-            if constexpr (MC) mc_store_4(P.exps + row, (uint32_t)e);
-            else P.exps[row] = e;
-        }
+        if (blockIdx.y == 0 && kc == 0) P.exps[row] = e;
         const bool finite = e != kNonFiniteExp;
         const int s = P.bits - e;
         const double f1 = pow2(s >> 1), f2 = pow2(s - (s >> 1));
@@ -300,11 +288,7 @@ __global__ void __launch_bounds__(256) split_strided_kernel(const __grid_constan
 #pragma unroll
         for (int j = 0; j < 16; ++j)
             v[j] = (finite && t0 + j < P.k) ? scale_round(tile[16 * kc + j][lr ^ ((kc & 7) << 2)], f1, f2) : 0.0;
-        store_chunk_residues<MC>(v, P.n_mod, P.res + row * P.res_ld + t0, P.res_plane);
-    }
-    if constexpr (MC) {
-        __syncthreads();
-        if (threadIdx.x == 0) mc_add_release(P.done, 1ull);
+        store_chunk_residues(v, P.n_mod, P.res + row * P.res_ld + t0, P.res_plane);
     }
 }
 

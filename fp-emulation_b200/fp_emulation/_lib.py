@@ -49,11 +49,9 @@ SIGNATURES = {
     "fpemu_gemm_crt_ex": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _i64, _vp, _vp, _int, _vp, _i64,
                                  _int, _vp, _int, _vp, _sz, _vp]),
     "fpemu_gemm_crt_noalloc": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _vp, _vp, _int, _vp, _i64, _vp]),
-    "fpemu_split_mc": (_int, [_i64, _i64, _vp, _i64, _i64, _int, _int, _vp, _i64, _i64, _vp, _vp, _vp, _vp]),
-    "fpemu_split_mc_signals": (_i64, [_i64, _i64]),
-    "fpemu_wait_counters": (_int, [_vp, _int, ctypes.c_uint64, _int, _vp]),
-    "fpemu_signal_counter": (_int, [_vp, _int, _vp]),
     "fpemu_device_error": (_int, [_IP, _IP, _IP, _IP, _int]),
+    "fpemu_watch_errors": (_int, []),
+    "fpemu_poll_error": (_int, [_IP, _IP, _IP, _IP]),
 }
 
 _lock = threading.Lock()
@@ -111,4 +109,29 @@ def device_error(clear: bool = True):
     lib = load()
     vals = [ctypes.c_int(0) for _ in range(4)]
     check(lib.fpemu_device_error(*[ctypes.byref(v) for v in vals], int(clear)), "device_error")
+    return tuple(v.value for v in vals)
+
+
+_watched = set()
+
+
+def watch(device_index: int) -> None:
+    """Once per device (which must be current): have this library's kernels also
+    record their first failure in pinned host memory, readable by poll_error()
+    without synchronising."""
+    if device_index in _watched:
+        return
+    with _lock:
+        if device_index not in _watched:
+            check(load().fpemu_watch_errors(), "fpemu_watch_errors")
+            _watched.add(device_index)
+
+
+def poll_error():
+    """(code, where, block, detail) of the first failure recorded on the current
+    device by kernels that have already finished; does not synchronise.  Needs
+    watch() on this device."""
+    lib = load()
+    vals = [ctypes.c_int(0) for _ in range(4)]
+    check(lib.fpemu_poll_error(*[ctypes.byref(v) for v in vals]), "poll_error")
     return tuple(v.value for v in vals)

@@ -11,8 +11,7 @@ The product is pipelined by column chunks of B: every rank runs the fused GEMM
 + CRT for chunk c (its rows x the chunk's columns of C) as soon as chunk c's
 residues are in its memory, while later chunks are in flight.  How they get
 there is the transport (TRANSPORT below): a copy-engine chain through CUDA IPC
-(default), a copy-engine ring of per-rank strips, NVLink multicast stores, or
-NCCL broadcasts.
+(default), a copy-engine ring of per-rank strips, or NCCL broadcasts.
 
 The NCCL pipeline is written against a small backend (`_GpuOps`) so that it
 can be exercised with CPU ranks over gloo in tests.
@@ -20,7 +19,6 @@ can be exercised with CPU ranks over gloo in tests.
 from __future__ import annotations
 
 import os
-import warnings
 from collections import OrderedDict
 from dataclasses import dataclass
 
@@ -42,11 +40,6 @@ BCAST_MODE = os.environ.get("FPEMU_BCAST", "residues")
 # How B's residues reach every rank:
 #  "ce" (default): the root splits B, copy engines relay the chunks along a chain
 #         of ranks through CUDA IPC (ce_transport.py);
-#  "nvls": every rank splits a strip of each column chunk and stores the residues
-#         through an NVLink multicast address (nvls_transport.py); falls back to
-#         "ce" where the group has no multicast support.  Opt-in: measured slower
-#         than "ce" at 8 GPUs (the multicast splits slow the concurrent GEMMs),
-#         and its counter waits timed out when a chunk's GEMM grid covered every SM;
 #  "ce-ring": every rank splits a strip of each chunk (FP64 strips copied from the
 #         root), the residue strips go round a ring by the copy engines
 #         (ce_transport.CeRing); bit-exact on 2 GPUs, not yet measured;
@@ -202,27 +195,6 @@ def _align256(x):
     return (x + 255) // 256 * 256
 
 
-def rowsharded_product_nvls(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, chunk_cols=CHUNK_COLS):
-    """Same product through the NVLS transport (nvls_transport.py)."""
-    from fp_emulation.nvls_transport import NvlsTransport
-
-    dev = A_local.device
-    plan = plan_column_chunks(n, chunk_cols)
-    key = ("nvls", root, dev.index, k, n, n_mod, tuple(plan))
-
-    def make():
-        try:
-            return NvlsTransport(group, root, dev, k, n, n_mod, _res_ld(k), plan)
-        except RuntimeError as exc:  # no multicast mapping for this group or size
-            raise _NvlsSetupError(str(exc)) from exc
-
-    return _cached_transport(group, key, make).product(A_local, B, ops, bits)
-
-
-class _NvlsSetupError(RuntimeError):
-    pass
-
-
 def rowsharded_product_ring(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, chunk_cols=CHUNK_COLS):
     """Same product through the copy-engine ring (ce_transport.CeRing): the root
     copies each rank its FP64 strip of every chunk, every rank splits its strip,
@@ -274,35 +246,15 @@ def rowsharded_product_ring(A_local, B, n, k, bits, n_mod, ops, root=0, group=No
     return C
 
 
-_NVLS_OK = {}
-
-
 def rowsharded_product_auto(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, transport=None):
-    """The product through the configured transport ("nvls" -> "ce" when the
-    group has no NVLink multicast)."""
+    """The product through the configured transport."""
     kind = transport or TRANSPORT
     if BCAST_MODE != "residues" or kind == "nccl":
         return rowsharded_product(A_local, B, n, k, bits, n_mod, ops, root, group)
     if kind == "ce-ring":
         return rowsharded_product_ring(A_local, B, n, k, bits, n_mod, ops, root, group)
-    if kind == "nvls":
-        gkey = id(group)
-        if gkey not in _NVLS_OK:
-            import torch.distributed._symmetric_memory  # noqa: F401  (multicast needs it)
-            from cuda.bindings import driver as drv
-
-            ok = drv.cuDeviceGetAttribute(drv.CUdevice_attribute.CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED,
-                                          A_local.device.index)[1] == 1
-            flags = [None] * dist.get_world_size(group)
-            dist.all_gather_object(flags, ok, group=group)
-            _NVLS_OK[gkey] = all(flags)
-        if _NVLS_OK[gkey]:
-            try:
-                return rowsharded_product_nvls(A_local, B, n, k, bits, n_mod, ops, root, group)
-            except _NvlsSetupError as exc:
-                warnings.warn(f"NVLS transport unavailable ({exc}); using the copy-engine chain")
-                _NVLS_OK[gkey] = False
-        kind = "ce"
+    if kind != "ce":
+        raise ValueError(f"unknown transport {kind!r} (ce, ce-ring, nccl)")
     return rowsharded_product_ce(A_local, B, n, k, bits, n_mod, ops, root, group, transport=kind)
 
 
@@ -393,5 +345,5 @@ def ozaki2_int8_matmul_rowsharded(A_local, B, n: int | None = None, root: int = 
         else:
             ops = _GpuOps(dev, comm_sms=None if TRANSPORT == "nccl" or BCAST_MODE != "residues" else 0)
             C = rowsharded_product_auto(A_local, B, n, k, bits, n_mod, ops, root, group)
-    _after_call("ozaki2_int8_matmul_rowsharded")
+    _after_call("ozaki2_int8_matmul_rowsharded", dev)
     return C if orig == torch.float64 else C.to(orig)

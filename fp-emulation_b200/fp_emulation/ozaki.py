@@ -34,7 +34,15 @@ _PRECISION_BITS = {
     torch.float64: 53,
 }
 
-_CHECK = os.environ.get("FPEMU_CHECK", "0") not in ("", "0")
+# How device-side failures (a bounded wait in a kernel that ran out) surface.
+# Such a failure also writes NaN over the output tiles the kernel could not finish.
+#   default ("poll"): every call ends by looking, without synchronising, at the
+#       host copy of the device's error record and raises FpemuError if a kernel
+#       that has already finished recorded one -- like an asynchronous CUDA
+#       error, a failure surfaces in the first call that ends after it happened;
+#   FPEMU_CHECK=1: also synchronise after every call and raise at once;
+#   FPEMU_CHECK=0: no check (the caller reads fp_emulation._lib.device_error()).
+_CHECK_MODE = {"0": "off", "1": "sync"}.get(os.environ.get("FPEMU_CHECK", ""), "poll")
 
 
 def _n_moduli(k, bits):
@@ -70,6 +78,9 @@ def _require_cuda(*tensors):
     for t in tensors[1:]:
         if t.device != dev:
             raise RuntimeError(f"operands on different devices: {dev} and {t.device}")
+    if _CHECK_MODE != "off" and dev.index not in _lib._watched:
+        with torch.cuda.device(dev):
+            _lib.watch(dev.index)
     return dev
 
 
@@ -77,13 +88,17 @@ def _res_ld(k: int) -> int:
     return ((k + 15) // 16) * 16
 
 
-def _after_call(what: str) -> None:
-    """With FPEMU_CHECK=1, synchronise and surface any device-side failure."""
-    if _CHECK:
+def _after_call(what: str, dev) -> None:
+    """Surface a device-side failure recorded on `dev` (see _CHECK_MODE)."""
+    if _CHECK_MODE == "off":
+        return
+    with torch.cuda.device(dev):
+        if _CHECK_MODE == "poll" and _lib.poll_error()[0] == 0:
+            return
         code, where, block, detail = _lib.device_error(clear=True)
-        if code:
-            raise _lib.FpemuError(code, f"{what}: device wait timed out (where={where} block={block} "
-                                        f"detail={detail})")
+    if code:
+        raise _lib.FpemuError(code, f"{what}: a kernel of fp_emulation on {dev} gave up waiting (where={where} "
+                                    f"block={block} detail={detail}); the outputs it could not finish are NaN")
 
 
 # ------------------------------------------------------------------ stages --
@@ -108,7 +123,7 @@ def _split(X, bits, n_mod):
                                      res.data_ptr(), ld, rows * ld, exps.data_ptr(),
                                      None if colmax is None else colmax.data_ptr(), _stream(dev))
     _lib.check(st, "_split")
-    _after_call("_split")
+    _after_call("_split", dev)
     return res, exps
 
 
@@ -133,7 +148,7 @@ def _matmul_residues(a_res, b_res, moduli, raw=False):
         st = _lib.load().fpemu_gemm_residues(m, n, k, n_mod, a_res.data_ptr(), b_res.data_ptr(), ld,
                                              0 if raw else 1, out.data_ptr(), None, 0, _stream(dev))
     _lib.check(st, "_matmul_residues")
-    _after_call("_matmul_residues")
+    _after_call("_matmul_residues", dev)
     return out
 
 
@@ -149,7 +164,7 @@ def _reconstruct(residues, moduli, bits, row_exp, col_exp):
         st = _lib.load().fpemu_crt_reconstruct(m, n, n_mod, res.data_ptr(), re.data_ptr(), ce.data_ptr(),
                                                bits, out.data_ptr(), n, _stream(dev))
     _lib.check(st, "_reconstruct")
-    _after_call("_reconstruct")
+    _after_call("_reconstruct", dev)
     return out
 
 
@@ -216,7 +231,7 @@ def _ozaki2_forward(A, B, n_mod=None, bias=None):
                 C.data_ptr(), n, c_dtype, None if fused_bias is None else fused_bias.data_ptr(), bits, n_mod,
                 ws.data_ptr(), ws.numel(), _stream(dev))
         _lib.check(st, "ozaki2_int8_matmul")
-        _after_call("ozaki2_int8_matmul")
+        _after_call("ozaki2_int8_matmul", dev)
     elif fused_bias is not None:
         C += fused_bias
     if C.dtype != orig_dtype:
@@ -247,7 +262,7 @@ def _gemm_crt_cached(A, b_res, col_exp, n_mod, bias=None):
                                        None if fused_bias is None else fused_bias.data_ptr(), 0, ws.data_ptr(),
                                        ws.numel(), _stream(dev))
         _lib.check(st, "ozaki2_int8_matmul (cached operand)")
-        _after_call("ozaki2_int8_matmul")
+        _after_call("ozaki2_int8_matmul", dev)
     elif fused_bias is not None:
         C += fused_bias
     return C

@@ -1,6 +1,6 @@
 """Column strips of B's chunks and the byte layout of the per-GPU buffer that
-holds them, shared by the transports in which every GPU splits one strip of
-each chunk (nvls_transport.py, and the copy-engine ring in ce_transport.py)."""
+holds them, for the transport in which every GPU splits one strip of each
+chunk (the copy-engine ring, ce_transport.CeRing)."""
 from __future__ import annotations
 
 import torch
@@ -19,8 +19,7 @@ def _even_split(w, parts, i):
 
 class StripLayout:
     """Byte layout of a GPU's buffer for one (world, k, n_mod, ld, plan):
-    [chunk 0 .. chunk nc-1 | staging slot 0 .. nc-1 | counters split/stage/gemm]
-    (the counters are the NVLS transport's; the ring transport stops before them).
+    [chunk 0 .. chunk nc-1 | staging slot 0 .. nc-1].
 
     chunk j: int8 residues [n_mod][w_j][ld] (plane stride w_j * ld), then the
     w_j int32 column exponents at res_bytes; strip q of chunk j is columns
@@ -39,11 +38,7 @@ class StripLayout:
         self.chunk_bytes = self.res_bytes + _align256(wmax * 4)
         self.slot_bytes = _align256(k * self.pitch * 8)
         self.stage_off = nc * self.chunk_bytes
-        self.cnt_off = self.stage_off + nc * self.slot_bytes
-        self.total = self.cnt_off + _align256(3 * nc * 8)
-
-    def counter(self, kind, j):
-        return self.cnt_off + 8 * (kind * len(self.plan) + j)
+        self.total = self.stage_off + nc * self.slot_bytes
 
     def residue_span(self, j, q):
         """[first, last] byte offsets the split of strip q of chunk j writes

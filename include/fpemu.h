@@ -174,47 +174,28 @@ int fpemu_gemm_crt_noalloc(int64_t m, int64_t n, int64_t k, int n_mod, const int
  * per-CTA residue staging). */
 size_t fpemu_gemm_workspace_size(int64_t m, int64_t n, int n_mod);
 
-/* ---- multi-GPU transport over NVLink multicast (NVLS) ------------------------
- * These have no counterpart in the reference, whose multi-GPU path broadcasts
- * B's residues with NCCL.  Here each GPU of the group splits a strip of every
- * column chunk of B and stores the residues through an NVLink multicast
- * address, so the switch writes them into every GPU's copy of the chunk.
- * Ordering between GPUs uses 64-bit counters that only grow. */
-
-/* Like fpemu_split for a strided X (s_k != 1), with res_mc and exps_mc NVLink
- * multicast addresses (the residues and exponents land on every GPU of the
- * group).  Each CTA of the residue kernel adds 1 to the multicast counter
- * *done_mc with release semantics after its stores, so a GPU whose copy of
- * the counter has grown by the producers' fpemu_split_mc_signals() totals holds
- * the whole chunk.  colmax_scratch: `rows` uint64 of this GPU's memory.  res_ld
- * must be k rounded up to 16. */
-int fpemu_split_mc(int64_t rows, int64_t k, const double *X, int64_t s_row, int64_t s_k, int bits,
-                   int n_mod, int8_t *res_mc, int64_t res_ld, int64_t res_plane, int32_t *exps_mc,
-                   uint64_t *colmax_scratch, uint64_t *done_mc, void *stream);
-
-/* How much one fpemu_split_mc call of this size adds to its counter. */
-int64_t fpemu_split_mc_signals(int64_t rows, int64_t k);
-
-/* Enqueue on `stream` a wait until each of the n (<= 16) counters (this GPU's,
- * or another GPU's through a peer mapping) is >= target; later work on the
- * stream sees what the counters' producers wrote before adding.  The wait is
- * bounded (FPEMU_WAIT_BUDGET_MS, default 2000 ms): on expiry it records
- * FPEMU_ERR_TIMEOUT for fpemu_device_error (detail = where * 16 + index) and
- * lets the stream continue. */
-int fpemu_wait_counters(const uint64_t *const *counters, int n, uint64_t target, int where,
-                        void *stream);
-
-/* Enqueue on `stream`: *counter += 1 (on every GPU of the group when
- * `multicast` is non-zero and counter is a multicast address) after all
- * earlier work on the stream. */
-int fpemu_signal_counter(uint64_t *counter, int multicast, void *stream);
-
 /* ---- device status ---------------------------------------------------------- */
 
 /* Synchronise the current device and read (optionally clear) the first error a
  * kernel of this library recorded on it (a bounded wait that timed out).
- * *code is FPEMU_OK when nothing was recorded.  where/block/detail may be NULL. */
+ * *code is FPEMU_OK when nothing was recorded.  where/block/detail may be NULL.
+ * When a GEMM wait times out, the output tiles the kernel could not finish are
+ * written as NaN, so a failed product never looks like a result.
+ * No counterpart in the reference (whose kernels have no waits); it replaces
+ * the TORCH_CHECK error path of crt_kernel.cu:63,75. */
 int fpemu_device_error(int *code, int *where, int *block, int *detail, int clear);
+
+/* Make the kernels of this library on the current device also record their
+ * first error in pinned host memory (allocated once per process; no device
+ * memory), so that fpemu_poll_error can see it without synchronising.  Call
+ * once per device, outside stream capture.  No counterpart in the reference. */
+int fpemu_watch_errors(void);
+
+/* Non-blocking: the first error recorded on the current device by kernels that
+ * have finished (FPEMU_OK if none so far).  Needs fpemu_watch_errors on this
+ * device; clear with fpemu_device_error(..., clear = 1).  No counterpart in the
+ * reference. */
+int fpemu_poll_error(int *code, int *where, int *block, int *detail);
 
 #ifdef __cplusplus
 }

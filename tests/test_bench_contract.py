@@ -42,3 +42,66 @@ def test_workload_configs():
     a = argparse.Namespace(config=2, n=16384, phi=1.0)
     c = bench.workload_config(a, 25, 1)
     assert (c["m"], c["n"], c["k"], c["phi"], c["parallelism"]) == (16384, 16384, 16384, 1.0, "single GPU")
+
+
+def _gate_worker(rank, world, port, plant, q):
+    import os
+    import traceback
+
+    try:
+        import numpy as np
+        import torch
+        import torch.distributed as dist
+
+        sys.path.insert(0, str(REPO))
+        import bench
+        from oracle import ozaki_oracle as oo
+
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        rng = np.random.default_rng(3)
+        m, k, n = 40, 96, 70
+        A = (rng.random((world * m, k)) - 0.5) * np.exp(rng.standard_normal((world * m, k)))
+        B = (rng.random((k, n)) - 0.5) * np.exp(rng.standard_normal((k, n)))
+        A_local = A[rank * m:(rank + 1) * m]
+        C = oo.ozaki2_matmul(A_local, B)
+        if plant and rank == world - 1:
+            C[-1, -1] = np.nextafter(C[-1, -1], np.inf)  # one ulp off in the last row and column
+        try:
+            res = bench.parity_gate(torch, dist, torch.from_numpy(A_local),
+                                    torch.from_numpy(B) if rank == 0 else None, torch.from_numpy(C), n, k,
+                                    world, rank, 0, torch.device("cpu"))
+            q.put((rank, "ok", res["status"]))
+        except RuntimeError as exc:
+            q.put((rank, "raised", str(exc)))
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, "error", traceback.format_exc()))
+
+
+def _run_gate(plant, world=2):
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s_:
+        s_.bind(("127.0.0.1", 0))
+        port = s_.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gate_worker, args=(r, world, port, plant, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = dict((r, (st, msg)) for r, st, msg in (q.get(timeout=120) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=30)
+    return out
+
+
+def test_parity_gate_passes_on_correct_shards_and_raises_everywhere_on_one_ulp():
+    """The bench's post-timing gate on 2 gloo ranks: exact shards pass; one ulp
+    planted in the last rank's last row and column makes every rank raise."""
+    good = _run_gate(plant=False)
+    assert all(st == "ok" and msg == "bit-exact" for st, msg in good.values()), good
+    bad = _run_gate(plant=True)
+    assert all(st == "raised" for st, _ in bad.values()), bad

@@ -9,7 +9,7 @@ import itertools
 import pytest
 
 from fp_emulation.distributed import plan_column_chunks
-from fp_emulation.nvls_transport import NvlsLayout, _even_split
+from fp_emulation.strips import StripLayout, _even_split
 from fp_emulation.ozaki import _res_ld
 
 
@@ -28,10 +28,10 @@ CASES = [(2, 700, 24, 1500, 512), (8, 700, 24, 1500, 512), (3, 129, 24, 751, 512
 
 
 @pytest.mark.parametrize("world,k,n_mod,n,chunk", CASES)
-def test_nvls_layout_writes_stay_in_their_regions(world, k, n_mod, n, chunk):
+def test_strip_layout_writes_stay_in_their_regions(world, k, n_mod, n, chunk):
     ld = _res_ld(k)
     plan = plan_column_chunks(n, chunk)
-    L = NvlsLayout(world, k, n_mod, ld, plan)
+    L = StripLayout(world, k, n_mod, ld, plan)
     assert L.pitch >= 2 and L.res_bytes % 256 == 0 and L.chunk_bytes % 256 == 0 and L.slot_bytes % 256 == 0
     for j, (c0, c1) in enumerate(plan):
         w = c1 - c0
@@ -47,7 +47,7 @@ def test_nvls_layout_writes_stay_in_their_regions(world, k, n_mod, n, chunk):
             (r0, r1), (e0, e1) = span
             assert lo_chunk <= r0 <= r1 < lo_chunk + L.res_bytes          # residues in the chunk's residue part
             assert lo_chunk + L.res_bytes <= e0 <= e1 < hi_chunk           # exponents after them
-            assert r0 % 16 == 0 and e0 % 4 == 0                           # multimem.st alignment
+            assert r0 % 16 == 0 and e0 % 4 == 0                           # 16-byte residue rows, int32 exponents
             s0, s1 = L.strips[j][q]
             # Each plane's rows of this strip: disjoint from the other strips' rows of that plane.
             res_spans.append((s0, s1))
@@ -56,21 +56,7 @@ def test_nvls_layout_writes_stay_in_their_regions(world, k, n_mod, n, chunk):
             assert slot0 <= a0 <= a1 < slot0 + L.slot_bytes
         for (a0, a1), (b0, b1) in itertools.combinations(res_spans, 2):
             assert a1 <= b0 or b1 <= a0
-    for kind, j in itertools.product(range(3), range(len(plan))):
-        off = L.counter(kind, j)
-        assert L.cnt_off <= off and off + 8 <= L.total and off % 8 == 0
-    assert L.stage_off == len(plan) * L.chunk_bytes and L.cnt_off == L.stage_off + len(plan) * L.slot_bytes
-
-
-def test_split_signal_count_matches_kernel_grid():
-    """The count each rank adds per chunk is the strided split's grid size, the
-    value the GEMM's wait targets are built from."""
-    from fp_emulation import _lib
-
-    lib = _lib.load()
-    for rows, k in [(1, 1), (32, 128), (33, 129), (256, 16384), (255, 8192), (60, 700)]:
-        res_ld = (k + 15) // 16 * 16
-        assert lib.fpemu_split_mc_signals(rows, k) == -(-rows // 32) * -(-res_ld // 128)
+    assert L.stage_off == len(plan) * L.chunk_bytes and L.total == L.stage_off + len(plan) * L.slot_bytes
 
 
 @pytest.mark.parametrize("world,k,n_mod,n,chunk", [(2, 70, 24, 600, 256), (3, 129, 24, 751, 512), (8, 33, 25, 300, 256)])
@@ -83,8 +69,8 @@ def test_strip_views_read_back_what_the_copies_wrote(world, k, n_mod, n, chunk):
 
     ld = _res_ld(k)
     plan = plan_column_chunks(n, chunk)
-    L = NvlsLayout(world, k, n_mod, ld, plan)
-    buf = torch.zeros(L.cnt_off, dtype=torch.int8)  # the ring's buffer stops before the counters
+    L = StripLayout(world, k, n_mod, ld, plan)
+    buf = torch.zeros(L.total, dtype=torch.int8)
     B = torch.randn(k, n, dtype=torch.float64)
     for j, (c0, c1) in enumerate(plan):
         res, exps = L.chunk_views(buf, j)
