@@ -54,7 +54,7 @@ SIGNATURES = {
     "fpemu_poll_error": (_int, [_IP, _IP, _IP, _IP]),
 }
 
-_lock = threading.Lock()
+_lock = threading.RLock()
 _lib = None
 
 
@@ -121,9 +121,10 @@ def watch(device_index: int) -> None:
     without synchronising."""
     if device_index in _watched:
         return
+    lib = load()
     with _lock:
         if device_index not in _watched:
-            check(load().fpemu_watch_errors(), "fpemu_watch_errors")
+            check(lib.fpemu_watch_errors(), "fpemu_watch_errors")
             _watched.add(device_index)
 
 

@@ -174,3 +174,41 @@ def test_transport_and_fusion_entry_points_validate_on_the_host():
     st = lib.fpemu_gemm_crt_ex(4, 4, 4, 24, None, None, 16, 64, None, None, 53, None, 4, 7, None, 0, None, 0, None)
     assert st == L.FPEMU_ERR_INVALID
     assert b"c_dtype" in lib.fpemu_last_error()
+
+
+def test_watch_loads_the_library_without_deadlock():
+    """The first library call of a process may be the one that arms the error
+    watch: _lib.watch must load the library itself without waiting on its own
+    lock.  Checked in a fresh process with the CUDA entry point replaced."""
+    import subprocess
+    import sys
+    import textwrap
+
+    code = textwrap.dedent(f"""
+        import sys, threading
+        sys.path.insert(0, {str(REPO / 'fp-emulation_b200')!r})
+        from fp_emulation import _lib
+        assert _lib._lib is None
+        calls = []
+        real_load = _lib.load
+
+        def load():
+            lib = real_load()
+            class Shim:
+                def __getattr__(self, name):
+                    return getattr(lib, name)
+                def fpemu_watch_errors(self):
+                    calls.append(1)
+                    return 0
+            return Shim()
+
+        _lib.load = load
+        t = threading.Thread(target=_lib.watch, args=(0,), daemon=True)
+        t.start()
+        t.join(20)
+        assert not t.is_alive(), "watch() deadlocked"
+        assert calls == [1] and 0 in _lib._watched
+        print("ok")
+    """)
+    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=60)
+    assert res.returncode == 0 and res.stdout.strip() == "ok", res.stdout + res.stderr
