@@ -5,6 +5,6 @@ Drop-in for the reference package's GEMM path (its ``__init__.py:1-13``):
 helpers (fit_pwl, eval_pwl, ...) are not part of this build.
 """
 from fp_emulation.nn import Linear, convert
-from fp_emulation.ozaki import ozaki2_int8_matmul
+from fp_emulation.ozaki import PreparedOperand, ozaki2_int8_matmul, prepare_operand
 
-__all__ = ["Linear", "convert", "ozaki2_int8_matmul"]
+__all__ = ["Linear", "convert", "ozaki2_int8_matmul", "PreparedOperand", "prepare_operand"]

@@ -3,7 +3,7 @@
 import torch
 from torch import nn
 
-from fp_emulation.ozaki import _gemm_crt_cached, _n_moduli, _ozaki2_forward, _split, ozaki2_int8_matmul
+from fp_emulation.ozaki import PreparedOperand, _ozaki2_forward, _ozaki2_forward_prepared, ozaki2_int8_matmul
 
 
 class Linear(nn.Linear):
@@ -21,20 +21,18 @@ class Linear(nn.Linear):
     def __init__(self, in_features, out_features, bias=True, device=None, cache_weight_residues=False):
         super().__init__(in_features, out_features, bias=bias, device=device, dtype=torch.float64)
         self.cache_weight_residues = cache_weight_residues
-        self._weight_split = None  # (key, b_res, col_exp)
+        self._weight_op = None  # (the weight Parameter it was made for, PreparedOperand of W^T)
 
     def _records_grad(self, x):
         return torch.is_grad_enabled() and (
             x.requires_grad or self.weight.requires_grad or (self.bias is not None and self.bias.requires_grad))
 
-    def _weight_residues(self, n_mod):
-        W = self.weight
-        key = (W.data_ptr(), W._version, W.device, n_mod)
-        if self._weight_split is None or self._weight_split[0] != key:
-            # W [out, in] row-major is B^T of the product: its rows are B's columns.
-            b_res, col_exp = _split(W.detach(), 53, n_mod)
-            self._weight_split = (key, b_res, col_exp)
-        return self._weight_split[1], self._weight_split[2]
+    def _weight_operand(self):
+        """W^T as a prepared right operand: W [out, in] row-major is B^T of the
+        product, so B's columns are W's rows (K contiguous)."""
+        if self._weight_op is None or self._weight_op[0] is not self.weight:
+            self._weight_op = (self.weight, PreparedOperand(self.weight.detach().T, "right"))
+        return self._weight_op[1]
 
     def forward(self, x):
         x = x.to(torch.float64)
@@ -47,9 +45,7 @@ class Linear(nn.Linear):
             if self.bias is not None:
                 y = y + self.bias
         elif self.cache_weight_residues and self.in_features > 0:
-            n_mod = _n_moduli(self.in_features, 53)
-            b_res, col_exp = self._weight_residues(n_mod)
-            y = _gemm_crt_cached(x2d, b_res, col_exp, n_mod, bias=self.bias)
+            y = _ozaki2_forward_prepared(x2d, self._weight_operand(), bias=self.bias)
         else:
             y = _ozaki2_forward(x2d, self.weight.T, bias=self.bias)
         return y.reshape(*lead, self.out_features)

@@ -195,20 +195,26 @@ def _fused_output(orig_dtype, bias, n, dev):
     return c_dtype, out_dtype, fused_bias
 
 
+def _dtype_bits(dtype):
+    """ozaki.py:97-104: the precision bits of a float dtype, TypeError otherwise."""
+    bits = _PRECISION_BITS.get(dtype)
+    if bits is None:
+        supported = ", ".join(str(d) for d in _PRECISION_BITS)
+        raise TypeError(
+            f"unsupported dtype {dtype}. "
+            f"CRT matmul emulates floating-point precision via int8 arithmetic; "
+            f"input must be a float type ({supported})"
+        )
+    return bits
+
+
 def _ozaki2_forward(A, B, n_mod=None, bias=None):
     """ozaki.py:95-119: scale -> modular INT8 matmuls -> CRT reconstruct, as one
     C call (split A, split B, fused GEMM + CRT) on the current stream.
     ``n_mod`` overrides the reference's modulus count (for sweeps).  ``bias``
     (n values) is added after the cast to the input's dtype -- nn.py:20-21's
     ``out + self.bias`` -- fused into the epilogue for float64/float32."""
-    bits = _PRECISION_BITS.get(A.dtype)
-    if bits is None:
-        supported = ", ".join(str(d) for d in _PRECISION_BITS)
-        raise TypeError(
-            f"unsupported dtype {A.dtype}. "
-            f"CRT matmul emulates floating-point precision via int8 arithmetic; "
-            f"input must be a float type ({supported})"
-        )
+    bits = _dtype_bits(A.dtype)
     dev = _require_cuda(A, B)
     if A.dim() != 2 or B.dim() != 2 or A.shape[1] != B.shape[0]:
         raise RuntimeError(f"ozaki2_int8_matmul: expected [m,k] @ [k,n], got {tuple(A.shape)} @ {tuple(B.shape)}")
@@ -241,19 +247,99 @@ def _ozaki2_forward(A, B, n_mod=None, bias=None):
     return C
 
 
-def _gemm_crt_cached(A, b_res, col_exp, n_mod, bias=None):
-    """C = A @ B from A (float64 [m, k], split here) and B's cached split
-    (b_res int8 [n_mod, n, ld], col_exp int32 [n]) -- the static-operand reuse
-    path; the result is what _ozaki2_forward(A, B, bias=bias) returns."""
-    dev = _require_cuda(A, b_res, col_exp)
-    bits = 53
-    m, k = A.shape
-    n = b_res.shape[1]
-    ld = b_res.shape[2]
-    c_dtype, out_dtype, fused_bias = _fused_output(torch.float64, bias, n, dev)
+class PreparedOperand:
+    """A static operand of ozaki2_int8_matmul whose split is kept on the GPU.
+
+    ``prepare_operand(X, "left")`` for the A of ``A @ B`` ([m, k]), or
+    ``prepare_operand(X, "right")`` for the B ([k, n]).  The first product that
+    uses it splits X (scaling exponents and int8 residues, ozaki.py:32-46) and
+    keeps the split -- n_mod bytes per element plus one int32 per row or column
+    -- so later products split only the other operand: the Chebyshev
+    differentiation matrix D of ``D @ u`` applied to new fields every epoch, or
+    the weight of a Linear layer.  The split is redone when X's storage or
+    version changes (an in-place update, an optimizer step) or the product needs
+    another modulus count or precision.  Results are bit-identical to the
+    unprepared product.  Under autograd the backward products use ``.T``, the
+    transposed operand, itself prepared on first use.  Not in the reference,
+    which splits both operands on every call."""
+
+    def __init__(self, X, side):
+        if side not in ("left", "right"):
+            raise ValueError(f"side must be 'left' or 'right', got {side!r}")
+        if not isinstance(X, torch.Tensor) or X.dim() != 2:
+            raise RuntimeError("a prepared operand is a 2-D tensor")
+        _dtype_bits(X.dtype)
+        _require_cuda(X)
+        self.tensor = X
+        self.side = side
+        self._split = None  # (key, residues, exponents)
+        self._t = None
+
+    @property
+    def shape(self):
+        return self.tensor.shape
+
+    @property
+    def dtype(self):
+        return self.tensor.dtype
+
+    @property
+    def device(self):
+        return self.tensor.device
+
+    @property
+    def T(self):
+        """The transposed operand, on the other side of a product (cached)."""
+        if self._t is None:
+            self._t = PreparedOperand(self.tensor.T, "right" if self.side == "left" else "left")
+            self._t._t = self
+        return self._t
+
+    def residues(self, n_mod, bits):
+        """(int8 residues [n_mod, rows, ld], int32 exponents [rows]) of the rows
+        of X (left) or the columns of X (right), split once per version."""
+        X = self.tensor
+        key = (X.data_ptr(), X._version, tuple(X.stride()), X.device, n_mod, bits)
+        if self._split is None or self._split[0] != key:
+            Xd = X.detach().double()
+            res, exps = _split(Xd if self.side == "left" else Xd.T, bits, n_mod)
+            self._split = (key, res, exps)
+        return self._split[1], self._split[2]
+
+
+def prepare_operand(X, side="left"):
+    """Keep the split of the static operand X on the GPU for repeated products
+    (see PreparedOperand)."""
+    return PreparedOperand(X, side)
+
+
+def _ozaki2_forward_prepared(A, B, bias=None):
+    """_ozaki2_forward where A and/or B is a PreparedOperand: the prepared side's
+    cached split, the other side split here, then the fused GEMM + CRT.  Same
+    dtype rules, output and bias handling as _ozaki2_forward."""
+    pa, pb = isinstance(A, PreparedOperand), isinstance(B, PreparedOperand)
+    if pa and A.side != "left":
+        raise ValueError("the left operand was prepared as a right operand")
+    if pb and B.side != "right":
+        raise ValueError("the right operand was prepared as a left operand")
+    At = A.tensor if pa else A
+    Bt = B.tensor if pb else B
+    bits = _dtype_bits(At.dtype)
+    dev = _require_cuda(At, Bt)
+    if At.dim() != 2 or Bt.dim() != 2 or At.shape[1] != Bt.shape[0]:
+        raise RuntimeError(f"ozaki2_int8_matmul: expected [m,k] @ [k,n], got {tuple(At.shape)} @ {tuple(Bt.shape)}")
+    orig_dtype = At.dtype
+    m, k = At.shape
+    n = Bt.shape[1]
+    if k == 0:
+        raise RuntimeError("ozaki2_int8_matmul: inner dimension k must be non-zero")
+    n_mod = _n_moduli(k, bits)
+    c_dtype, out_dtype, fused_bias = _fused_output(orig_dtype, bias, n, dev)
     C = torch.empty((m, n), dtype=out_dtype, device=dev)
     if m and n:
-        a_res, row_exp = _split(A, bits, n_mod)
+        a_res, row_exp = A.residues(n_mod, bits) if pa else _split(At.double(), bits, n_mod)
+        b_res, col_exp = B.residues(n_mod, bits) if pb else _split(Bt.double().T, bits, n_mod)
+        ld = a_res.shape[2]
         lib = _lib.load()
         with torch.cuda.device(dev):
             ws = torch.empty((max(lib.fpemu_gemm_workspace_size(m, n, n_mod), 256),), dtype=torch.uint8, device=dev)
@@ -261,10 +347,14 @@ def _gemm_crt_cached(A, b_res, col_exp, n_mod, bias=None):
                                        row_exp.data_ptr(), col_exp.data_ptr(), bits, C.data_ptr(), n, c_dtype,
                                        None if fused_bias is None else fused_bias.data_ptr(), 0, ws.data_ptr(),
                                        ws.numel(), _stream(dev))
-        _lib.check(st, "ozaki2_int8_matmul (cached operand)")
+        _lib.check(st, "ozaki2_int8_matmul (prepared operand)")
         _after_call("ozaki2_int8_matmul", dev)
     elif fused_bias is not None:
         C += fused_bias
+    if C.dtype != orig_dtype:
+        C = C.to(orig_dtype)
+    if bias is not None and fused_bias is None:
+        C = C + bias
     return C
 
 
@@ -287,10 +377,41 @@ class _OzakiMatmul(torch.autograd.Function):
         return grad_A, grad_B
 
 
+class _OzakiMatmulPrepared(torch.autograd.Function):
+    """_OzakiMatmul with one or both operands prepared; the backward products use
+    the prepared transposes (ozaki.py:132-136 otherwise)."""
+
+    @staticmethod
+    def forward(A_t, B_t, A_op, B_op):
+        return _ozaki2_forward_prepared(A_op, B_op)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        A_t, B_t, A_op, B_op = inputs
+        ctx.save_for_backward(A_t, B_t)
+        ctx.ops = (A_op, B_op)
+
+    @staticmethod
+    def backward(ctx, grad):
+        A_t, B_t = ctx.saved_tensors
+        A_op, B_op = ctx.ops
+        B_T = B_op.T if isinstance(B_op, PreparedOperand) else B_t.T
+        A_T = A_op.T if isinstance(A_op, PreparedOperand) else A_t.T
+        grad_A = ozaki2_int8_matmul(grad, B_T) if ctx.needs_input_grad[0] else None
+        grad_B = ozaki2_int8_matmul(A_T, grad) if ctx.needs_input_grad[1] else None
+        return grad_A, grad_B, None, None
+
+
 def ozaki2_int8_matmul(A, B):
     """
     FP-accurate matmul via INT8 tensor cores (Ozaki scheme II + CRT).
 
     Precision matches input dtype (fp16, bf16, fp32, fp64).  CUDA tensors only.
+    Either operand may be a PreparedOperand (prepare_operand), whose split is
+    reused across calls.
     """
+    if isinstance(A, PreparedOperand) or isinstance(B, PreparedOperand):
+        A_t = A.tensor if isinstance(A, PreparedOperand) else A
+        B_t = B.tensor if isinstance(B, PreparedOperand) else B
+        return _OzakiMatmulPrepared.apply(A_t, B_t, A, B)
     return _OzakiMatmul.apply(A, B)

@@ -212,3 +212,21 @@ def test_watch_loads_the_library_without_deadlock():
     """)
     res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=60)
     assert res.returncode == 0 and res.stdout.strip() == "ok", res.stdout + res.stderr
+
+
+def test_prepared_operand_validates_on_the_host():
+    """prepare_operand keeps the public op's rules: CUDA tensors only, 2-D,
+    float dtypes (TypeError otherwise), and a side of 'left' or 'right'."""
+    import pytest
+    import torch
+
+    from fp_emulation import prepare_operand
+
+    with pytest.raises(ValueError):
+        prepare_operand(torch.zeros(2, 2, dtype=torch.float64), "middle")
+    with pytest.raises(TypeError):
+        prepare_operand(torch.zeros(2, 2, dtype=torch.int32), "left")
+    with pytest.raises(RuntimeError, match="CUDA"):
+        prepare_operand(torch.zeros(2, 2, dtype=torch.float64), "left")
+    with pytest.raises(RuntimeError):
+        prepare_operand(torch.zeros(2, dtype=torch.float64), "left")

@@ -98,13 +98,13 @@ def test_linear_weight_cache_reuse_and_invalidation(torch_cuda):
     x = torch.randn(33, 257, dtype=torch.float64, generator=torch.Generator().manual_seed(4)).cuda()
     with torch.no_grad():
         y1 = lin(x)
-        first = lin._weight_split[1]
+        first = lin._weight_op[1]._split[1]
         y2 = lin(x)
-        assert lin._weight_split[1] is first, "an unchanged weight must reuse its split"
+        assert lin._weight_op[1]._split[1] is first, "an unchanged weight must reuse its split"
         assert torch.equal(y1, y2)
         lin.weight.mul_(-0.5)  # in place: bumps the version
         y3 = lin(x)
-        assert lin._weight_split[1] is not first, "an in-place update must re-split the weight"
+        assert lin._weight_op[1]._split[1] is not first, "an in-place update must re-split the weight"
     W = lin.weight.detach().cpu().numpy()
     want = oo.ozaki2_matmul(x.cpu().numpy(), W.T) + lin.bias.detach().cpu().numpy()
     np.testing.assert_array_equal(y3.cpu().numpy().view(np.int64), want.view(np.int64))
