@@ -289,9 +289,10 @@ class PreparedOperand:
 
     @property
     def T(self):
-        """The transposed operand, on the other side of a product (cached)."""
+        """The transposed operand, prepared for the same side (cached): the
+        backward of ``A @ B`` computes ``A.T @ grad`` and ``grad @ B.T``."""
         if self._t is None:
-            self._t = PreparedOperand(self.tensor.T, "right" if self.side == "left" else "left")
+            self._t = PreparedOperand(self.tensor.T, self.side)
             self._t._t = self
         return self._t
 

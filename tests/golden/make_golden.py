@@ -26,14 +26,21 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF_SRC = Path("/root/reference/src")
+# The reference's ``src`` directory (the parent of its fp_emulation package):
+# FPEMU_REFERENCE_SRC names its fp_emulation directory, else the copy installed
+# in baseline/_ref is used.
+REF_SRC = (Path(os.environ["FPEMU_REFERENCE_SRC"]).parent if os.environ.get("FPEMU_REFERENCE_SRC")
+           else REPO / "baseline" / "_ref")
 
 # Stage tensors larger than this many elements are stored as digests + samples.
 FULL_LIMIT = 40_000
 
 
 def _setup_reference():
-    os.environ["LIBRARY_PATH"] = "/usr/lib/gcc/x86_64-linux-gnu/13:" + os.environ.get("LIBRARY_PATH", "")
+    sys.path.insert(0, str(REPO))
+    from oracle.build_oracle import gcc_libdir
+
+    os.environ["LIBRARY_PATH"] = gcc_libdir() + ":" + os.environ.get("LIBRARY_PATH", "")
     os.environ.setdefault("TORCH_EXTENSIONS_DIR", str(REPO / "oracle" / "_build" / "torch_ext"))
     sys.path.insert(0, str(REF_SRC))
     import fp_emulation.ozaki as oz  # the reference package
