@@ -60,6 +60,10 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-extras", action="store_true", help="skip DGEMM/cuBLASLt/CPU side numbers")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) leg")
+    ap.add_argument("--b-layout", choices=["root", "sharded"], default="root",
+                    help="N > 1, the timed product: B held by rank 0 (its residues sent to every rank; default) "
+                         "or column-sharded (rank q holds columns [q*n/N, (q+1)*n/N) and the residues are "
+                         "all-gathered).  The end-to-end leg at N > 1 always uses the column-sharded public op")
     return ap.parse_args()
 
 
@@ -83,7 +87,8 @@ def workload_config(args, n_mod, world, transport=None):
         "l2": f"inputs larger than L2 ({8 * M * K / 2**30:.1f} and {8 * K * N / 2**30:.1f} GiB operands); no flush",
         "parallelism": "single GPU" if world == 1 else (
             f"A row-sharded over {world} GPUs, B residues to every GPU over NVLink "
-            f"({transport or os.environ.get('FPEMU_TRANSPORT', 'ce')} transport, "
+            f"({transport or os.environ.get('FPEMU_TRANSPORT', 'ce')}"
+            f"{'' if 'column-sharded' in str(transport) else ' transport, B on rank 0'}, "
             f"{os.environ.get('FPEMU_BCAST', 'residues')})"),
     }
 
@@ -204,7 +209,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     from fp_emulation import _lib
-    from fp_emulation.distributed import ozaki2_int8_matmul_rowsharded, shard_rows
+    from fp_emulation.distributed import ozaki2_int8_matmul_allgather, shard_rows
     from fp_emulation.ozaki import _n_moduli, _res_ld, ozaki2_int8_matmul
 
     world, rank, local = dist_env()
@@ -223,13 +228,22 @@ def run_ours(args):
     ld = _res_ld(k)
     root = 0
 
+    sharded = world > 1 and args.b_layout == "sharded"
+    if world > 1 and n % world:
+        raise SystemExit(f"n = {n} must be a multiple of the GPU count")
+    nb = n // world
+    # Every rank draws the same B (one seeded generator), so that the column-sharded
+    # layouts below hold the root's values; rank 0 keeps all of it.
     if args.config == 3:
         A = synth_config3_rows(torch, M, r0, r1, k, args.seed + 1 + rank, dev)
         B = torch.randn(k, n, dtype=torch.float64, device=dev,
-                        generator=torch.Generator(device=dev).manual_seed(args.seed + 1000)) if rank == root else None
+                        generator=torch.Generator(device=dev).manual_seed(args.seed + 1000))
     else:
         A = synth(torch, m, k, args.phi, args.seed + 1 + rank, dev)
-        B = synth(torch, k, n, args.phi, args.seed + 1000, dev) if rank == root else None
+        B = synth(torch, k, n, args.phi, args.seed + 1000, dev)
+    B_block = B[:, rank * nb:(rank + 1) * nb].contiguous() if world > 1 else None
+    if world > 1 and rank != root and not sharded:
+        B = None
 
     a_res = torch.empty((n_mod, m, ld), dtype=torch.int8, device=dev)
     b_res = torch.empty((n_mod, n, ld), dtype=torch.int8, device=dev) if (world == 1 or rank == root) else None
@@ -260,7 +274,10 @@ def run_ours(args):
         dist_ops.timing = gemm_timing if record else None
         first = len(gemm_timing)
         if ev: ev[0].record(stream)
-        last_step["C"] = product(A, B, n, k, bits, n_mod, dist_ops, root=root)
+        if sharded:
+            last_step["C"] = fdist.rowsharded_product_allgather(A, B_block, k, bits, n_mod, dist_ops)
+        else:
+            last_step["C"] = product(A, B, n, k, bits, n_mod, dist_ops, root=root)
         if ev:
             ev[1].record(stream)
             n_steps_events.append(ev + [first, len(gemm_timing)])
@@ -334,6 +351,8 @@ def run_ours(args):
     transport_used = None
     if world > 1:
         transport_used = fdist.TRANSPORT if fdist.BCAST_MODE == "residues" else "nccl"
+        if sharded:
+            transport_used = "column-sharded B, residues all-gathered by the copy-engine ring"
     flops = 2.0 * M * n * k
     value = flops / (ms_step * 1e-3) / 1e12
 
@@ -380,6 +399,8 @@ def run_ours(args):
     # chunk the strip's 2 split kernels and one GEMM.
     if world == 1:
         per_rank = 4
+    elif sharded:
+        per_rank = 1 + 3 * len(fdist.plan_column_chunks(nb, fdist.allgather_strip_cols(world)))
     elif transport_used == "ce-ring":
         per_rank = 1 + 3 * n_chunks
     else:
@@ -394,11 +415,15 @@ def run_ours(args):
         # copied host->device (pinned) while step i computes, and step i's C is
         # copied device->host behind it.  Every step still moves its full inputs
         # and its full result across PCIe inside the timed region.
+        # One GPU: the public op on A and B.  N GPUs: the column-sharded public op,
+        # each rank copying in only its rows of A and its block of B's columns
+        # (every GPU's PCIe link carries its share; B whole on one rank would put
+        # all of B's bytes through the root's link every step).
         A_h = A.cpu().pin_memory()
-        B_h = B.cpu().pin_memory() if rank == root else None
+        B_h = (B if world == 1 else B_block).cpu().pin_memory()
         C_h = [torch.empty((m, n), dtype=torch.float64).pin_memory() for _ in range(2)]
         A_d = [torch.empty_like(A) for _ in range(2)]
-        B_d = [torch.empty((k, n), dtype=torch.float64, device=dev) if rank == root else None for _ in range(2)]
+        B_d = [torch.empty(tuple(B_h.shape), dtype=torch.float64, device=dev) for _ in range(2)]
         del a_res  # give the public op's own workspace room
         h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         loaded = [torch.cuda.Event() for _ in range(2)]
@@ -410,8 +435,7 @@ def run_ours(args):
             with torch.cuda.stream(h2d):
                 h2d.wait_event(consumed[b])          # the previous step using buffer b is done
                 A_d[b].copy_(A_h, non_blocking=True)
-                if rank == root:
-                    B_d[b].copy_(B_h, non_blocking=True)
+                B_d[b].copy_(B_h, non_blocking=True)
                 loaded[b].record(h2d)
 
         def run(i):
@@ -420,7 +444,7 @@ def run_ours(args):
             if world == 1:
                 Cd = ozaki2_int8_matmul(A_d[b], B_d[b])
             else:
-                Cd = ozaki2_int8_matmul_rowsharded(A_d[b], B_d[b], n=n, root=root)
+                Cd = ozaki2_int8_matmul_allgather(A_d[b], B_d[b])
             consumed[b].record(stream)
             with torch.cuda.stream(d2h):
                 d2h.wait_event(consumed[b])
@@ -448,12 +472,15 @@ def run_ours(args):
         torch.cuda.synchronize(dev)
         barrier()
         e2e_ms = max_over_ranks(s2.elapsed_time(t2)) / e2e_steps
-        h2d_bytes = sum_over_ranks(A_h.numel() * 8 + (B_h.numel() * 8 if B_h is not None else 0))
+        h2d_bytes = sum_over_ranks(A_h.numel() * 8 + B_h.numel() * 8)
         d2h_bytes = sum_over_ranks(C_h[0].numel() * 8)
         e2e = {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
                "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": int(d2h_bytes),
                "ms_per_step": round(e2e_ms, 3),
-               "method": "public op per step; H2D of step i+1 and D2H of step i overlap step i's compute"}
+               "method": ("public op per step" if world == 1 else
+                          "column-sharded public op (ozaki2_int8_matmul_allgather) per step: each rank copies in "
+                          "its rows of A and its column block of B") +
+                         "; H2D of step i+1 and D2H of step i overlap step i's compute"}
         # Sanity guard on the last end-to-end result: a row sample against cuBLAS DGEMM.
         if world == 1:
             b = last["b"]

@@ -525,6 +525,11 @@ int bits_ok(int bits) {
     return FPEMU_OK;
 }
 
+int gemm_crt_impl(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_res, const int8_t* b_res,
+                  int64_t res_ld, int64_t b_res_plane, const int32_t* row_exp, const int32_t* col_exp, int bits,
+                  void* C, int64_t ldc, int c_dtype, const void* bias, int col_seg, int64_t col_seg_stride,
+                  int max_ctas, void* workspace, size_t workspace_bytes, void* stream);
+
 }  // namespace
 
 // ==================================================================== C ABI ==
@@ -668,6 +673,32 @@ int fpemu_gemm_crt_ex(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* 
                       int64_t res_ld, int64_t b_res_plane, const int32_t* row_exp, const int32_t* col_exp, int bits,
                       void* C, int64_t ldc, int c_dtype, const void* bias, int max_ctas, void* workspace,
                       size_t workspace_bytes, void* stream) {
+    return gemm_crt_impl(m, n, k, n_mod, a_res, b_res, res_ld, b_res_plane, row_exp, col_exp, bits, C, ldc, c_dtype,
+                         bias, 0, 0, max_ctas, workspace, workspace_bytes, stream);
+}
+
+int fpemu_gemm_crt_segmented(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_res, const int8_t* b_res,
+                             int64_t res_ld, int64_t b_res_plane, const int32_t* row_exp, const int32_t* col_exp,
+                             int bits, double* C, int64_t ldc, int64_t col_seg, int64_t col_seg_stride, int max_ctas,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+    if (col_seg < 1 || col_seg > 0x7FFFFFFFll || col_seg_stride < col_seg)
+        return fail(FPEMU_ERR_INVALID, "gemm_crt_segmented: col_seg=%lld, col_seg_stride=%lld (need 1 <= col_seg <= "
+                    "col_seg_stride)", (long long)col_seg, (long long)col_seg_stride);
+    if (n > 0 && ((n - 1) / col_seg) * col_seg_stride + (n - 1) % col_seg >= ldc)
+        return fail(FPEMU_ERR_INVALID, "gemm_crt_segmented: the last column lands past ldc=%lld", (long long)ldc);
+    return gemm_crt_impl(m, n, k, n_mod, a_res, b_res, res_ld, b_res_plane, row_exp, col_exp, bits, C, ldc,
+                         FPEMU_C_F64, nullptr, (int)col_seg, col_seg_stride, max_ctas, workspace, workspace_bytes,
+                         stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+int gemm_crt_impl(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_res, const int8_t* b_res,
+                  int64_t res_ld, int64_t b_res_plane, const int32_t* row_exp, const int32_t* col_exp, int bits,
+                  void* C, int64_t ldc, int c_dtype, const void* bias, int col_seg, int64_t col_seg_stride,
+                  int max_ctas, void* workspace, size_t workspace_bytes, void* stream) {
     if (c_dtype != FPEMU_C_F64 && c_dtype != FPEMU_C_F32)
         return fail(FPEMU_ERR_INVALID, "c_dtype=%d: expected FPEMU_C_F64 (0) or FPEMU_C_F32 (1)", c_dtype);
     if (bias != nullptr && reinterpret_cast<uintptr_t>(bias) % (c_dtype == FPEMU_C_F32 ? 4 : 8) != 0)
@@ -693,6 +724,8 @@ int fpemu_gemm_crt_ex(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* 
     P.ldc = ldc;
     P.bias = bias;
     P.c_f32 = c_dtype == FPEMU_C_F32;
+    P.col_seg = col_seg;
+    P.col_seg_stride = col_seg_stride;
     P.row_exp = row_exp;
     P.col_exp = col_exp;
     P.two_bits = 2 * bits;
@@ -708,6 +741,10 @@ int fpemu_gemm_crt_ex(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* 
     return launch_gemm<kModeCrt>(P, a_res, b_res, res_ld, b_res_plane, d, static_cast<cudaStream_t>(stream),
                                  max_ctas);
 }
+
+}  // namespace
+
+extern "C" {
 
 int fpemu_gemm_crt_noalloc(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_res,
                            const int8_t* b_res, int64_t res_ld, const int32_t* row_exp,

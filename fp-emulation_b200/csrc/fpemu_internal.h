@@ -71,6 +71,8 @@ struct GemmParams {
     int64_t ldc;
     const void* bias;      // mode 2, optional: per-column bias in C's type, added after the cast
     int c_f32;             // mode 2: C is float (the double result rounded to nearest)
+    int col_seg;           // mode 2: > 0 scatters column j of this product to C column
+    int64_t col_seg_stride;  //   (j / col_seg) * col_seg_stride + j % col_seg; 0 keeps column j
     const int32_t* row_exp;
     const int32_t* col_exp;
     int two_bits;

@@ -89,17 +89,25 @@ __device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, ui
     return a | (b << 8) | (c << 16) | (d << 24);
 }
 
+// C column of column j of this product: j itself, or -- for a product over
+// columns gathered from several column blocks of C -- segment j / col_seg of
+// width col_seg, col_seg_stride apart.
+__device__ __forceinline__ int64_t out_col(const GemmParams& P, int j) {
+    return P.col_seg > 0 ? (int64_t)(j / P.col_seg) * P.col_seg_stride + j % P.col_seg : (int64_t)j;
+}
+
 // Write one reconstructed value: the double result, or its round-to-nearest
 // float when C is float32, then the optional per-column bias added in C's type
 // -- the order of the reference's `matmul(...).to(dtype)` followed by `+ bias`.
 __device__ __forceinline__ void store_c(const GemmParams& P, double* crow, int64_t row, int col, double v) {
+    const int64_t oc = out_col(P, col);
     if (P.c_f32) {
         float f = __double2float_rn(v);
         if (P.bias) f = __fadd_rn(f, static_cast<const float*>(P.bias)[col]);
-        reinterpret_cast<float*>(P.C)[row * P.ldc + col] = f;
+        reinterpret_cast<float*>(P.C)[row * P.ldc + oc] = f;
     } else {
         if (P.bias) v = __dadd_rn(v, static_cast<const double*>(P.bias)[col]);
-        crow[col] = v;
+        crow[oc] = v;
     }
 }
 
@@ -447,8 +455,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 const int col0 = tn * BN + cg * Cfg::kCols;
 #pragma unroll 1
                 for (int c = 0; c < Cfg::kCols && col0 + c < P.n; ++c) {
-                    if (P.c_f32) reinterpret_cast<float*>(P.C)[row * P.ldc + col0 + c] = __double2float_rn(qnan);
-                    else P.C[row * P.ldc + col0 + c] = qnan;
+                    const int64_t oc = out_col(P, col0 + c);
+                    if (P.c_f32) reinterpret_cast<float*>(P.C)[row * P.ldc + oc] = __double2float_rn(qnan);
+                    else P.C[row * P.ldc + oc] = qnan;
                 }
             }
         }

@@ -48,6 +48,8 @@ SIGNATURES = {
                                     _int, _int, _vp, _sz, _vp]),
     "fpemu_gemm_crt_ex": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _i64, _vp, _vp, _int, _vp, _i64,
                                  _int, _vp, _int, _vp, _sz, _vp]),
+    "fpemu_gemm_crt_segmented": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _i64, _vp, _vp, _int, _vp, _i64,
+                                        _i64, _i64, _int, _vp, _sz, _vp]),
     "fpemu_gemm_crt_noalloc": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _vp, _vp, _int, _vp, _i64, _vp]),
     "fpemu_device_error": (_int, [_IP, _IP, _IP, _IP, _int]),
     "fpemu_watch_errors": (_int, []),

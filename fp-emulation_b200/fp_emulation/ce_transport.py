@@ -337,8 +337,12 @@ class CeRing(_IpcChunks):
 
     EVENTS = ("stage", "have")
 
-    def __init__(self, group, root, device, layout):
+    def __init__(self, group, root, device, layout, staged=True):
+        """staged=False: no root staging -- every rank splits its strips from its
+        own copy of its part of B (a column-sharded B), and only the ring moves
+        data between GPUs."""
         self.layout = layout
+        self.staged = staged
         nc = len(layout.plan)
         super().__init__(group, root, device, layout.chunk_bytes, nc, extra_bytes=nc * layout.slot_bytes)
         W = self.world
@@ -349,7 +353,7 @@ class CeRing(_IpcChunks):
         self.split_stream = self._new_stream()
         self.copy_stream = self._new_stream()
         self.ring = [self._new_stream() for _ in range(W - 1)]  # step t on ring[t - 1]
-        self.phases = ("stage", "split") + tuple(f"ring{t}" for t in range(1, W))
+        self.phases = (("stage",) if staged else ()) + ("split",) + tuple(f"ring{t}" for t in range(1, W))
 
     def _events_per_chunk(self, name):
         return self.world if name == "have" else 1
@@ -393,17 +397,23 @@ class CeRing(_IpcChunks):
             self._record(cs, self._stage(c))
         self._publish("stage")
 
-    def split_own(self, split_fn):
+    def split_own(self, split_fn, main_stream=None):
         """Every rank: split_fn(c, stream) enqueues on `stream` the split of this
-        rank's FP64 strip of chunk c (staging slot c) into its residue strip."""
+        rank's FP64 strip of chunk c (staging slot c, or the rank's own part of B
+        when unstaged) into its residue strip.  Unstaged, the split stream first
+        waits for `main_stream`, where the caller produced its part of B."""
         i = self.calls
-        self._wait_keys([self.root], i, "stage")
+        if self.staged:
+            self._wait_keys([self.root], i, "stage")
         if i > 0 and self.world > 1:
             self._wait_keys([self.succ], i - 1, "ring1")
         ss = self.split_stream
+        if not self.staged and main_stream is not None:
+            ss.wait_stream(main_stream)
         for c in range(len(self.layout.plan)):
             ss.wait_event(self.gemm_done[c])
-            self._wait(ss, self._stage(c), "stage")
+            if self.staged:
+                self._wait(ss, self._stage(c), "stage")
             if i > 0 and self.world > 1:  # succ pulled this strip at its step 1
                 self._wait(ss, self._have(self.succ, c, self.rank), "split war")
             split_fn(c, ss)

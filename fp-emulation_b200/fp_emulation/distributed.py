@@ -117,6 +117,26 @@ class _GpuOps:
             self.timing.append((ev[0], ev[1], 2.0 * m * w * k * n_mod))
 
 
+    def gemm_crt_segmented(self, a_res, re, b_res, ce_chunk, bits, C, col_off, seg, seg_stride, k):
+        """C[:, cols] for one all-gathered chunk: chunk column j goes to C column
+        col_off + (j // seg) * seg_stride + j % seg."""
+        n_mod, m, ld = a_res.shape
+        w = b_res.shape[1]
+        nbytes = self.lib.fpemu_gemm_workspace_size(m, w, n_mod)
+        ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=self.device)
+        if self.timing is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        st = self.lib.fpemu_gemm_crt_segmented(m, w, k, n_mod, a_res.data_ptr(), b_res.data_ptr(), ld,
+                                               b_res.stride(0), re.data_ptr(), ce_chunk.data_ptr(), bits,
+                                               C.data_ptr() + 8 * col_off, C.stride(0), seg, seg_stride,
+                                               self.max_ctas, ws.data_ptr(), ws.numel(), _stream(self.device))
+        _lib.check(st, "gemm_crt_segmented")
+        if self.timing is not None:
+            ev[1].record()
+            self.timing.append((ev[0], ev[1], 2.0 * m * w * k * n_mod))
+
+
 def rowsharded_product(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, chunk_cols=CHUNK_COLS,
                        mode=None):
     """The pipeline: chunked split/broadcast of B's residues (or of B itself,
@@ -310,6 +330,97 @@ def rowsharded_product_ce(A_local, B, n, k, bits, n_mod, ops, root=0, group=None
             ops.gemm_crt(a_res, row_exp, res, exps, bits, C, c0, c1, k)
         tr.after_gemm(c, stream)
     return C
+
+
+def allgather_strip_cols(world, chunk_cols=CHUNK_COLS):
+    """Columns each GPU contributes to one chunk of the all-gathered product
+    (CHUNK_COLS across the group, a multiple of 16)."""
+    return max(16, (chunk_cols // world) // 16 * 16)
+
+
+def rowsharded_product_allgather(A_local, B_local, k, bits, n_mod, ops, group=None, strip_cols=None):
+    """C_local = A_local @ B with B column-sharded: this rank holds columns
+    [q*nb, (q+1)*nb) of B as B_local [k, nb].  Chunk c gathers strip
+    [c*sw, c*sw + w_c) of every rank's block; each rank splits its own strips
+    (no root), the residue strips go round the copy-engine ring (CeRing,
+    unstaged), and the GEMM of chunk c writes each strip's columns to their
+    place in C through the segmented epilogue."""
+    from fp_emulation.ce_transport import CeRing
+    from fp_emulation.strips import StripLayout
+
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    dev = A_local.device
+    m = A_local.shape[0]
+    nb = B_local.shape[1]
+    ld = _res_ld(k)
+    sw = strip_cols or allgather_strip_cols(world)
+    key = ("allgather", dev.index, k, nb, n_mod, sw)
+
+    def make():
+        # Collective: every rank must hold a block of the same shape.
+        shapes = [None] * world
+        dist.all_gather_object(shapes, (k, nb, n_mod), group=group)
+        if any(x != shapes[0] for x in shapes):
+            raise RuntimeError(f"column-sharded B: every rank needs a [k, nb] block of one shape, got {shapes}")
+        return CeRing(group, 0, dev, StripLayout.for_blocks(world, k, n_mod, ld, nb, sw), staged=False)
+
+    tr = _cached_transport(group, key, make)
+    L = tr.layout
+    stream = torch.cuda.current_stream(dev)
+    B_local.record_stream(tr.split_stream)
+
+    def split_fn(c, ss):
+        s0, s1 = L.strips[c][rank]
+        res, exps = L.chunk_views(tr.buf, c)
+        X = B_local[:, L.block_off[c]: L.block_off[c] + (s1 - s0)].T  # the strip's columns as rows, K strided
+        with torch.cuda.stream(ss):
+            ops.split(X, bits, n_mod, res[:, s0:s1, :], exps[s0:s1])
+
+    tr.split_own(split_fn, main_stream=stream)
+    tr.ring_steps()
+    a_res = ops.empty_res(n_mod, m, ld)
+    row_exp = ops.empty_exps(m)
+    ops.split(A_local, bits, n_mod, a_res, row_exp)
+    C = torch.empty((m, world * nb), dtype=torch.float64, device=dev)
+    for c, (c0, c1) in enumerate(L.plan):
+        res, exps = L.chunk_views(tr.buf, c)
+        tr.wait_chunk(c, stream)
+        if m and c1 > c0:
+            ops.gemm_crt_segmented(a_res, row_exp, res, exps, bits, C, L.block_off[c], L.strips[c][0][1], nb, k)
+        tr.after_gemm(c, stream)
+    return C
+
+
+def ozaki2_int8_matmul_allgather(A_local, B_local, group=None):
+    """C_local = A_local @ B with A row-sharded and B column-sharded across the
+    ranks of `group`: rank q passes its rows of A and its block of columns
+    [q*nb, (q+1)*nb) of B (every rank the same nb), and gets its rows of C over
+    all world*nb columns (float64, or A's dtype), bit-identical to the
+    single-GPU product.  B's residues are all-gathered over NVLink by the copy
+    engines, pipelined with the GEMMs.  Called collectively, in the same order on
+    every rank.  Not in the reference, which has no multi-GPU path."""
+    bits = _PRECISION_BITS.get(A_local.dtype)
+    if bits is None:
+        raise TypeError(f"unsupported dtype {A_local.dtype}")
+    dev = _require_cuda(A_local, B_local)
+    orig = A_local.dtype
+    A_local, B_local = A_local.double(), B_local.double()
+    k = A_local.shape[1]
+    if B_local.dim() != 2 or B_local.shape[0] != k:
+        raise RuntimeError(f"B_local must be [k, nb] with k = {k}, got {tuple(B_local.shape)}")
+    if k == 0:
+        raise RuntimeError("inner dimension k must be non-zero")
+    n_mod = _n_moduli(k, bits)
+    with torch.cuda.device(dev):
+        if dist.get_world_size(group) == 1:
+            from fp_emulation.ozaki import _ozaki2_forward
+
+            C = _ozaki2_forward(A_local, B_local, n_mod=n_mod)
+        else:
+            C = rowsharded_product_allgather(A_local, B_local, k, bits, n_mod, _GpuOps(dev, comm_sms=0), group)
+    _after_call("ozaki2_int8_matmul_allgather", dev)
+    return C if orig == torch.float64 else C.to(orig)
 
 
 def ozaki2_int8_matmul_rowsharded(A_local, B, n: int | None = None, root: int = 0, group=None):

@@ -26,19 +26,45 @@ class StripLayout:
     strips[j][q] of the chunk.  Staging slot j: rank's FP64 strip, k rows of
     `pitch` doubles (pitch >= 2 keeps the split's K stride non-unit)."""
 
-    def __init__(self, world, k, n_mod, ld, plan):
+    def __init__(self, world, k, n_mod, ld, plan, strips=None, staging=True):
         self.world, self.k, self.n_mod, self.ld, self.plan = world, k, n_mod, ld, plan
         nc = len(plan)
-        self.strips = [[_even_split(c1 - c0, world, q) for q in range(world)] for c0, c1 in plan]
+        self.strips = strips or [[_even_split(c1 - c0, world, q) for q in range(world)] for c0, c1 in plan]
         wmax = max(c1 - c0 for c0, c1 in plan)
         swmax = max(s1 - s0 for row in self.strips for s0, s1 in row)
         self.swmax = swmax
         self.pitch = max(swmax, 2)
         self.res_bytes = _align256(n_mod * wmax * ld)
         self.chunk_bytes = self.res_bytes + _align256(wmax * 4)
-        self.slot_bytes = _align256(k * self.pitch * 8)
+        self.slot_bytes = _align256(k * self.pitch * 8) if staging else 0
         self.stage_off = nc * self.chunk_bytes
         self.total = self.stage_off + nc * self.slot_bytes
+        self.block_cols = None  # set by for_blocks
+        self.block_off = None
+
+    @classmethod
+    def for_blocks(cls, world, k, n_mod, ld, block_cols, strip_cols):
+        """Layout for B column-sharded in equal blocks of `block_cols` columns
+        (GPU q holds columns [q*block_cols, (q+1)*block_cols) of B).  Chunk c
+        gathers columns [c*strip_cols, c*strip_cols + w_c) of every GPU's block,
+        w_c = min(strip_cols, block_cols - c*strip_cols): strip q of chunk c is
+        GPU q's piece, columns [q*w_c, (q+1)*w_c) of the chunk.  No staging slots
+        (every GPU splits its own block).  `plan` lists the chunks' column ranges
+        as if the chunks were laid side by side; block_off[c] = c*strip_cols is
+        where chunk c starts inside each block."""
+        if block_cols < 1 or strip_cols < 1:
+            raise ValueError("block and strip widths must be positive")
+        plan, strips, offs, off = [], [], [], 0
+        for c0 in range(0, block_cols, strip_cols):
+            w = min(strip_cols, block_cols - c0)
+            plan.append((off, off + world * w))
+            strips.append([(q * w, (q + 1) * w) for q in range(world)])
+            offs.append(c0)
+            off += world * w
+        L = cls(world, k, n_mod, ld, plan, strips=strips, staging=False)
+        L.block_cols = block_cols
+        L.block_off = offs
+        return L
 
     def residue_span(self, j, q):
         """[first, last] byte offsets the split of strip q of chunk j writes

@@ -145,6 +145,19 @@ int fpemu_gemm_crt_ex(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t *
                       int64_t ldc, int c_dtype, const void *bias, int max_ctas, void *workspace,
                       size_t workspace_bytes, void *stream);
 
+/* fpemu_gemm_crt for a product whose columns come from several column blocks
+ * of C: column j of this product is written to C column
+ *     (j / col_seg) * col_seg_stride + j % col_seg
+ * (1 <= col_seg <= col_seg_stride).  The multi-GPU product over a
+ * column-sharded B uses it: a column chunk of the all-gathered B holds one
+ * strip of col_seg columns from each GPU's block of col_seg_stride columns.
+ * No counterpart in the reference (which has no multi-GPU path). */
+int fpemu_gemm_crt_segmented(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t *a_res,
+                             const int8_t *b_res, int64_t res_ld, int64_t b_res_plane,
+                             const int32_t *row_exp, const int32_t *col_exp, int bits, double *C,
+                             int64_t ldc, int64_t col_seg, int64_t col_seg_stride, int max_ctas,
+                             void *workspace, size_t workspace_bytes, void *stream);
+
 /* Allocation-free variant of fpemu_gemm_crt.  It has no counterpart in the
  * reference.  For callers that cannot allocate device memory -- code running
  * where cudaMalloc is not allowed (inside a host application that owns the

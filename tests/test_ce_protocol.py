@@ -230,7 +230,7 @@ def test_chain_waits_bind_to_the_right_records(world, root):
 _PREVIOUS_CALL = {"stage war", "split war", "ring war", "gemm"}
 
 
-def _ring_worker(rank, world, port, root, calls, n_chunks, q):
+def _ring_worker(rank, world, port, root, calls, n_chunks, q, staged=True):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         import torch.distributed as dist
@@ -265,16 +265,20 @@ def _ring_worker(rank, world, port, root, calls, n_chunks, q):
                 fake.label = what
                 return super()._wait(stream, event, what)
 
-        plan = plan_column_chunks(256 * n_chunks - 100, 256)  # a ragged last chunk
-        layout = StripLayout(world, 300, 24, 304, plan)
-        ring = FakeRing(None, root, None, layout)
+        if staged:
+            plan = plan_column_chunks(256 * n_chunks - 100, 256)  # a ragged last chunk
+            layout = StripLayout(world, 300, 24, 304, plan)
+        else:  # column blocks of 90 columns, strips of 32: chunks of 32, 32 and 26 per rank
+            layout = StripLayout.for_blocks(world, 300, 24, 304, 32 * n_chunks - 6, 32)
+            plan = layout.plan
+        ring = FakeRing(None, root, None, layout, staged=staged)
         fake.chain = ring
         splits = []
         main = _Stream()
         for _ in range(calls):
-            if rank == root:
+            if rank == root and staged:
                 ring.root_stage(0x1000, 256 * n_chunks, main)
-            ring.split_own(lambda c, ss: splits.append(c))
+            ring.split_own(lambda c, ss: splits.append(c), main_stream=main)
             ring.ring_steps()
             for c in range(len(plan)):
                 ring.wait_chunk(c, main)
@@ -289,13 +293,18 @@ def _ring_worker(rank, world, port, root, calls, n_chunks, q):
         q.put((rank, "error", traceback.format_exc()))
 
 
+@pytest.mark.parametrize("staged", [True, False], ids=["root-staged", "column-sharded"])
 @pytest.mark.parametrize("world,root", [(2, 1), (3, 0), (4, 3)])
-def test_ring_waits_bind_to_the_right_records(world, root):
+def test_ring_waits_bind_to_the_right_records(world, root, staged):
+    """Root-staged: the root copies every rank its FP64 strip.  Column-sharded
+    (the all-gather product): every rank splits its own block, nothing is staged."""
     calls, n_chunks = 4, 3
+    if not staged:
+        root = 0
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ring_worker, args=(r, world, port, root, calls, n_chunks, q))
+    procs = [ctx.Process(target=_ring_worker, args=(r, world, port, root, calls, n_chunks, q, staged))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -313,8 +322,8 @@ def test_ring_waits_bind_to_the_right_records(world, root):
                 assert owner == (pred if label == "ring" else succ), (rank, owner, label)
             counts[label] = counts.get(label, 0) + 1
         W = world
-        assert counts.get("stage war", 0) == (W * nc * (calls - 1) if rank == root else 0)
-        assert counts["stage"] == nc * calls
+        assert counts.get("stage war", 0) == (W * nc * (calls - 1) if rank == root and staged else 0)
+        assert counts.get("stage", 0) == (nc * calls if staged else 0)
         assert counts.get("split war", 0) == nc * (calls - 1)
         assert counts["ring"] == (W - 1) * nc * calls
         assert counts.get("ring war", 0) == (W - 2) * nc * (calls - 1)
@@ -322,7 +331,7 @@ def test_ring_waits_bind_to_the_right_records(world, root):
         assert n_splits == nc * calls
         # 2-D copies: the root's FP64 strips (W per chunk) and the ring's residue strips;
         # 1-D copies: the ring's column exponents.
-        assert copies2d == (W * nc * calls if rank == root else 0) + (W - 1) * nc * calls
+        assert copies2d == (W * nc * calls if rank == root and staged else 0) + (W - 1) * nc * calls
         assert copies == (W - 1) * nc * calls
         assert left == [calls - 2, calls - 1], left
 

@@ -67,8 +67,6 @@ def test_rowsharded_multi_gpu_bit_exact(transport, world, tmp_path):
     import torch.multiprocessing as mp
 
     have = torch.cuda.device_count()
-    if transport == "ce-ring" and world == "all":
-        pytest.skip("the copy-engine ring has been run on 2 GPUs only so far")
     if world == "all":
         if have < 3:
             pytest.skip("needs 3 or more GPUs")
@@ -99,3 +97,65 @@ def test_rowsharded_multi_gpu_bit_exact(transport, world, tmp_path):
     np.testing.assert_array_equal(C.view(np.int64), want.view(np.int64))
     # Column exponents are per column, so the product with B[:, :n2] is C[:, :n2].
     np.testing.assert_array_equal(C2.view(np.int64), want[:, :n2].view(np.int64))
+
+
+def _allgather_worker(rank, world, store_file, m, k, nb, q):
+    try:
+        import torch
+
+        os.environ.update(NCCL_NVLS_ENABLE="0", FPEMU_CHUNK_COLS="256")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        torch.distributed.init_process_group("nccl", init_method=f"file://{store_file}", rank=rank,
+                                             world_size=world, device_id=dev, timeout=timedelta(seconds=60))
+        from fp_emulation import _lib
+        from fp_emulation.distributed import ozaki2_int8_matmul_allgather, shard_rows
+
+        A, B = _problem(m, k, world * nb)
+        r0, r1 = shard_rows(m, world, rank)
+        A_local = torch.from_numpy(A[r0:r1]).to(dev)
+        B_local = torch.from_numpy(np.ascontiguousarray(B[:, rank * nb:(rank + 1) * nb])).to(dev)
+        for _ in range(2):  # buffers, events and store keys reused by the second call
+            C = ozaki2_int8_matmul_allgather(A_local, B_local)
+        torch.cuda.synchronize(dev)
+        code = _lib.device_error(clear=True)
+        q.put((rank, "ok", (r0, r1, C.cpu().numpy(), code)))
+        torch.distributed.barrier(device_ids=[rank])
+        torch.distributed.destroy_process_group()
+    except Exception:
+        q.put((rank, "error", traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world", [2, "all"])
+def test_allgather_product_column_sharded_b_bit_exact(world, tmp_path):
+    """A row-sharded, B column-sharded (rank q holds columns [q*nb, (q+1)*nb));
+    blocks of 250 columns cut into strips of 256 // world columns, so the last
+    chunk is narrower.  The gathered rows of C equal the oracle's full product."""
+    import torch
+    import torch.multiprocessing as mp
+
+    have = torch.cuda.device_count()
+    if world == "all":
+        if have < 3:
+            pytest.skip("needs 3 or more GPUs")
+        world = have
+    elif have < world:
+        pytest.skip(f"needs {world} GPUs")
+    m, k, nb = 900, 700, 250
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    store_file = str(tmp_path / "store")
+    procs = [ctx.Process(target=_allgather_worker, args=(r, world, store_file, m, k, nb, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    C = np.full((m, world * nb), np.nan)
+    for rank, status, payload in results:
+        assert status == "ok", payload
+        r0, r1, Cr, code = payload
+        assert code[0] == 0, code
+        C[r0:r1] = Cr
+    A, B = _problem(m, k, world * nb)
+    np.testing.assert_array_equal(C.view(np.int64), oo.ozaki2_matmul(A, B).view(np.int64))

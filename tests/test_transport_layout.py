@@ -88,3 +88,24 @@ def test_strip_views_read_back_what_the_copies_wrote(world, k, n_mod, n, chunk):
                              dtype=torch.int8)
         assert torch.equal(res[0, :, 0], owner) and torch.equal(res[-1, :, -1], owner)
         assert torch.equal(exps, owner.to(torch.int32) + 999)
+
+
+@pytest.mark.parametrize("world,k,n_mod,block,strip", [(2, 700, 24, 250, 80), (8, 16384, 25, 2048, 256),
+                                                       (3, 129, 24, 17, 16), (4, 64, 24, 1, 256)])
+def test_column_block_layout_covers_every_column_once(world, k, n_mod, block, strip):
+    """The all-gather layout: chunk c holds strip q = GPU q's columns
+    [block_off[c], block_off[c] + w_c) of its block; the segmented epilogue sends
+    chunk column j to C column block_off[c] + (j // w_c) * block + j % w_c.  Every
+    column of C is written exactly once, by the chunk holding that GPU's piece."""
+    L = StripLayout.for_blocks(world, k, n_mod, _res_ld(k), block, strip)
+    assert L.slot_bytes == 0 and L.total == len(L.plan) * L.chunk_bytes
+    hit = [0] * (world * block)
+    for c, (c0, c1) in enumerate(L.plan):
+        w = L.strips[c][0][1]
+        assert c1 - c0 == world * w and L.strips[c] == [(q * w, (q + 1) * w) for q in range(world)]
+        for j in range(c1 - c0):
+            col = L.block_off[c] + (j // w) * block + j % w
+            q = j // w
+            assert q * block <= col < (q + 1) * block  # GPU q's block
+            hit[col] += 1
+    assert hit == [1] * (world * block)
