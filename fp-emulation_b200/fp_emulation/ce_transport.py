@@ -337,12 +337,18 @@ class CeRing(_IpcChunks):
 
     EVENTS = ("stage", "have")
 
-    def __init__(self, group, root, device, layout, staged=True):
+    def __init__(self, group, root, device, layout, staged=True, pieces=None):
         """staged=False: no root staging -- every rank splits its strips from its
         own copy of its part of B (a column-sharded B), and only the ring moves
-        data between GPUs."""
+        data between GPUs.  `pieces` (FPEMU_RING_PIECES, default 4): each ring
+        step moves a strip as that many groups of modulus planes, each with its
+        own event, so the next hop starts on the first group instead of waiting
+        for the whole strip (the first chunk's fill shrinks from W-1 strip copies
+        to W-1 piece copies plus one strip)."""
         self.layout = layout
         self.staged = staged
+        P = int(os.environ.get("FPEMU_RING_PIECES", "4")) if pieces is None else pieces
+        self.pieces = max(1, min(layout.n_mod, P))
         nc = len(layout.plan)
         super().__init__(group, root, device, layout.chunk_bytes, nc, extra_bytes=nc * layout.slot_bytes)
         W = self.world
@@ -356,14 +362,22 @@ class CeRing(_IpcChunks):
         self.phases = (("stage",) if staged else ()) + ("split",) + tuple(f"ring{t}" for t in range(1, W))
 
     def _events_per_chunk(self, name):
-        return self.world if name == "have" else 1
+        return self.world * self.pieces if name == "have" else 1
 
     def _phases(self):
         return self.phases
 
-    def _have(self, owner, c, q):
+    def _have(self, owner, c, q, p=None):
+        """Event `owner` records once piece p of strip q of chunk c is in its buffer;
+        p defaults to the last piece, recorded after all the others on the same stream."""
+        p = self.pieces - 1 if p is None else p
         evs = self.ev["have"] if owner == self.rank else self.peer_events(owner, "have")
-        return evs[c * self.world + q]
+        return evs[(c * self.world + q) * self.pieces + p]
+
+    def plane_pieces(self):
+        """[(first plane, end plane)] of each piece: n_mod planes in near-equal groups."""
+        n, P = self.layout.n_mod, self.pieces
+        return [(p * n // P, (p + 1) * n // P) for p in range(P)]
 
     def _stage(self, c):
         evs = self.ev["stage"] if self.rank == self.root else self.peer_events(self.root, "stage")
@@ -417,7 +431,8 @@ class CeRing(_IpcChunks):
             if i > 0 and self.world > 1:  # succ pulled this strip at its step 1
                 self._wait(ss, self._have(self.succ, c, self.rank), "split war")
             split_fn(c, ss)
-            self._record(ss, self._have(self.rank, c, self.rank))
+            for p in range(self.pieces):  # the split wrote every piece of this rank's strip
+                self._record(ss, self._have(self.rank, c, self.rank, p))
         self._publish("split")
 
     def ring_steps(self):
@@ -432,21 +447,25 @@ class CeRing(_IpcChunks):
                 self._wait_keys([self.succ], i - 1, f"ring{t + 1}")
             rs = self.ring[t - 1]
             s = self.strip_at(t)
+            pieces = self.plane_pieces()
             for c, (c0, c1) in enumerate(L.plan):
                 rs.wait_event(self.gemm_done[c])
-                self._wait(rs, self._have(self.pred, c, s), "ring")
-                if war:
-                    self._wait(rs, self._have(self.succ, c, s), "ring war")
                 s0, s1 = L.strips[c][s]
-                if s1 > s0:
-                    w = c1 - c0
-                    base = c * L.chunk_bytes
-                    # residues: rows s0..s1 of each of the n_mod planes (plane stride w*ld)
-                    self._copy2d(rs, int(self.ptr) + base + s0 * L.ld, w * L.ld,
-                                 self.peer_ptr(self.pred) + base + s0 * L.ld, w * L.ld, (s1 - s0) * L.ld, L.n_mod)
-                    off = base + L.res_bytes + 4 * s0  # column exponents
-                    self._copy(rs, int(self.ptr) + off, self.peer_ptr(self.pred) + off, 4 * (s1 - s0))
-                self._record(rs, self._have(self.rank, c, s))
+                w = c1 - c0
+                base = c * L.chunk_bytes
+                for p, (l0, l1) in enumerate(pieces):
+                    self._wait(rs, self._have(self.pred, c, s, p), "ring")
+                    if war:
+                        self._wait(rs, self._have(self.succ, c, s, p), "ring war")
+                    if s1 > s0:
+                        # residues: rows s0..s1 of planes l0..l1 (plane stride w*ld)
+                        off = base + l0 * w * L.ld + s0 * L.ld
+                        self._copy2d(rs, int(self.ptr) + off, w * L.ld, self.peer_ptr(self.pred) + off, w * L.ld,
+                                     (s1 - s0) * L.ld, l1 - l0)
+                        if p == len(pieces) - 1:
+                            off = base + L.res_bytes + 4 * s0  # column exponents
+                            self._copy(rs, int(self.ptr) + off, self.peer_ptr(self.pred) + off, 4 * (s1 - s0))
+                    self._record(rs, self._have(self.rank, c, s, p))
             self._publish(f"ring{t}")
         # Every rank that waits on this rank's keys of call i-2 has passed those
         # waits (they sit in calls i-2 and i-1 of the neighbours and the root,

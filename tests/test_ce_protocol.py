@@ -286,7 +286,7 @@ def _ring_worker(rank, world, port, root, calls, n_chunks, q, staged=True):
         dist.barrier()
         left = [i for i in range(calls) if store.check([ring._key(rank, i, "split")])]
         q.put((rank, "ok", (ring.pred, ring.succ, fake.waits, fake.copies, fake.copies2d, len(splits), left,
-                            len(plan))))
+                            len(plan), ring.pieces)))
         dist.barrier()
         dist.destroy_process_group()
     except Exception:
@@ -313,7 +313,7 @@ def test_ring_waits_bind_to_the_right_records(world, root, staged):
         p.join(timeout=60)
     for rank, status, payload in results:
         assert status == "ok", payload
-        pred, succ, waits, copies, copies2d, n_splits, left, nc = payload
+        pred, succ, waits, copies, copies2d, n_splits, left, nc, P = payload
         counts = {}
         for owner, _idx, seen, at_call, label in waits:
             want = at_call if label in _PREVIOUS_CALL else at_call + 1
@@ -325,13 +325,14 @@ def test_ring_waits_bind_to_the_right_records(world, root, staged):
         assert counts.get("stage war", 0) == (W * nc * (calls - 1) if rank == root and staged else 0)
         assert counts.get("stage", 0) == (nc * calls if staged else 0)
         assert counts.get("split war", 0) == nc * (calls - 1)
-        assert counts["ring"] == (W - 1) * nc * calls
-        assert counts.get("ring war", 0) == (W - 2) * nc * (calls - 1)
+        assert counts["ring"] == (W - 1) * nc * calls * P
+        assert counts.get("ring war", 0) == (W - 2) * nc * (calls - 1) * P
         assert counts["gemm"] == W * nc * calls
         assert n_splits == nc * calls
         # 2-D copies: the root's FP64 strips (W per chunk) and the ring's residue strips;
         # 1-D copies: the ring's column exponents.
-        assert copies2d == (W * nc * calls if rank == root and staged else 0) + (W - 1) * nc * calls
+        assert P == 4
+        assert copies2d == (W * nc * calls if rank == root and staged else 0) + (W - 1) * nc * calls * P
         assert copies == (W - 1) * nc * calls
         assert left == [calls - 2, calls - 1], left
 
