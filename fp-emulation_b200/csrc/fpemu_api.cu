@@ -84,6 +84,21 @@ int device_info(DevInfo* out) {
     return FPEMU_OK;
 }
 
+// Split of a K-contiguous operand: 1 = both passes in one kernel (the row is
+// re-read from L2), 2 = an exponent kernel, then a residue kernel
+// (FPEMU_SPLIT_ROWS).  Under mode 1, FPEMU_SPLIT_CTAS caps the CTAs per SM, and
+// so the rows in flight whose second pass must find them in L2.
+int split_rows_mode() {
+    const char* s = getenv("FPEMU_SPLIT_ROWS");
+    return (s && atoi(s) == 2) ? 2 : 1;
+}
+
+int split_rows_ctas_per_sm() {
+    const char* s = getenv("FPEMU_SPLIT_CTAS");
+    const int v = s ? atoi(s) : 64;
+    return v < 1 ? 1 : (v > 64 ? 64 : v);
+}
+
 // Test hook of the failure-detection tests (FPEMU_TEST_STALL_UNIT=i): the TMA
 // producers of the GEMM's first unit stop delivering at their unit i, so the
 // consumers' bounded waits run out exactly as they would behind a stalled
@@ -362,12 +377,20 @@ int launch_split(const SplitParams& P, uint64_t* colmax, const DevInfo& d, cudaS
         const int group = P.k <= 512 ? 32 : P.k <= 2048 ? 64 : P.k <= 8192 ? 128 : 256;
         const int64_t rows_per_cta = 256 / group;
         int64_t grid = (P.rows + rows_per_cta - 1) / rows_per_cta;
-        const int64_t cap = (int64_t)d.sms * 64;
+        const int two = split_rows_mode() == 2;
+        const int64_t cap = (int64_t)d.sms * (two ? 64 : split_rows_ctas_per_sm());
         if (grid > cap) grid = cap;
-#define FPEMU_SPLIT_ROWS(G)                                                                     \
-    do {                                                                                        \
-        if (vec) split_rows_kernel<G, true><<<(unsigned)grid, 256, 0, st>>>(P);                 \
-        else split_rows_kernel<G, false><<<(unsigned)grid, 256, 0, st>>>(P);                    \
+#define FPEMU_SPLIT_ROWS(G)                                                                      \
+    do {                                                                                         \
+        if (two) {                                                                               \
+            if (vec) split_rowexp_kernel<G, true><<<(unsigned)grid, 256, 0, st>>>(P);            \
+            else split_rowexp_kernel<G, false><<<(unsigned)grid, 256, 0, st>>>(P);               \
+            if (vec) split_rowres_kernel<G, true><<<(unsigned)grid, 256, 0, st>>>(P);            \
+            else split_rowres_kernel<G, false><<<(unsigned)grid, 256, 0, st>>>(P);               \
+        } else {                                                                                 \
+            if (vec) split_rows_kernel<G, true><<<(unsigned)grid, 256, 0, st>>>(P);              \
+            else split_rows_kernel<G, false><<<(unsigned)grid, 256, 0, st>>>(P);                 \
+        }                                                                                        \
     } while (0)
         switch (group) {
             case 32: FPEMU_SPLIT_ROWS(32); break;

@@ -142,86 +142,134 @@ __device__ __forceinline__ void store_chunk_residues(const double (&x)[16], int 
 // row; each thread walks chunks of 16 elements, stride GROUP chunks.
 // VEC: the row start is 16-byte aligned, so chunks load as 8 x 16 bytes.
 // ---------------------------------------------------------------------------
+
+// This thread's share of max |x| over a row, as the bit pattern of the
+// magnitude (monotone for non-negative doubles; NaN patterns sort above Inf).
+template <int GROUP, bool VEC>
+__device__ __forceinline__ unsigned long long row_maxbits_part(const double* x, int64_t k, int gt) {
+    unsigned long long mb = 0;
+    const int64_t nchunk = (k + 15) / 16;
+    for (int64_t c = gt; c < nchunk; c += GROUP) {
+        const int64_t t0 = c * 16;
+        if (VEC && t0 + 16 <= k) {
+            const double2* p2 = reinterpret_cast<const double2*>(x + t0);
+            double2 d[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) d[j] = __ldg(p2 + j);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                mb = max(mb, (unsigned long long)__double_as_longlong(d[j].x) & 0x7FFFFFFFFFFFFFFFull);
+                mb = max(mb, (unsigned long long)__double_as_longlong(d[j].y) & 0x7FFFFFFFFFFFFFFFull);
+            }
+        } else {
+            for (int j = 0; j < 16 && t0 + j < k; ++j) {
+                const double d = __ldg(x + t0 + j);
+                mb = max(mb, (unsigned long long)__double_as_longlong(d) & 0x7FFFFFFFFFFFFFFFull);
+            }
+        }
+    }
+    return mb;
+}
+
+// Max over the GROUP threads of a row slot (g = the slot in this CTA); every
+// thread of the CTA must call it (it synchronises the CTA when GROUP > 32).
+template <int GROUP>
+__device__ __forceinline__ unsigned long long row_max_reduce(unsigned long long mb, int g,
+                                                             unsigned long long* red) {
+    constexpr int kWarps = GROUP / 32;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+    if (kWarps > 1) {
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = mb;
+        __syncthreads();
+        mb = 0;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) mb = max(mb, red[g * kWarps + w]);
+        __syncthreads();
+    }
+    return mb;
+}
+
+// Residues of one row whose exponent e is known: every chunk of the row, all
+// moduli (columns k..res_ld-1 written as zero).
+template <int GROUP, bool VEC>
+__device__ __forceinline__ void row_residues(const SplitParams& P, const double* x, int64_t row, int e, int gt) {
+    const bool finite = e != kNonFiniteExp;
+    const int s = P.bits - e;
+    const double f1 = pow2(s >> 1), f2 = pow2(s - (s >> 1));
+    const int64_t nchunk_out = P.res_ld / 16;
+    int8_t* out_row = P.res + row * P.res_ld;
+    for (int64_t c = gt; c < nchunk_out; c += GROUP) {
+        const int64_t t0 = c * 16;
+        double v[16];
+        if (finite && VEC && t0 + 16 <= P.k) {
+            const double2* p2 = reinterpret_cast<const double2*>(x + t0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const double2 d = __ldg(p2 + j);
+                v[2 * j] = scale_round(d.x, f1, f2);
+                v[2 * j + 1] = scale_round(d.y, f1, f2);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                v[j] = (finite && t0 + j < P.k) ? scale_round(__ldg(x + t0 + j), f1, f2) : 0.0;
+        }
+        store_chunk_residues(v, P.n_mod, out_row + t0, P.res_plane);
+    }
+}
+
+// Two passes per row in one kernel: the row maximum, then (re-reading the row,
+// from L2 when it is still there) the residues.
 template <int GROUP, bool VEC>
 __global__ void __launch_bounds__(256) split_rows_kernel(const __grid_constant__ SplitParams P) {
     static_assert(GROUP % 32 == 0 && 256 % GROUP == 0, "bad group");
     constexpr int kRowsPerCta = 256 / GROUP;
-    constexpr int kWarps = GROUP / 32;
     __shared__ unsigned long long red[256 / 32];
-
-    const int g = threadIdx.x / GROUP;       // row slot in this CTA
-    const int gt = threadIdx.x % GROUP;      // thread within the row group
-    const int warp_in_group = gt / 32;
-    const int64_t nchunk_in = (P.k + 15) / 16;
-    const int64_t nchunk_out = P.res_ld / 16;
-
+    const int g = threadIdx.x / GROUP;   // row slot in this CTA
+    const int gt = threadIdx.x % GROUP;  // thread within the row group
     for (int64_t row0 = (int64_t)blockIdx.x * kRowsPerCta; row0 < P.rows;
          row0 += (int64_t)gridDim.x * kRowsPerCta) {
         const int64_t row = row0 + g;
         const bool live = row < P.rows;
         const double* x = P.X + (live ? row : 0) * P.s_row;
-
-        // Pass 1: max |x| as the bit pattern of the magnitude (monotone for
-        // non-negative doubles; NaN patterns sort above Inf).
-        unsigned long long mb = 0;
-        if (live) {
-            for (int64_t c = gt; c < nchunk_in; c += GROUP) {
-                const int64_t t0 = c * 16;
-                if (VEC && t0 + 16 <= P.k) {
-                    const double2* p2 = reinterpret_cast<const double2*>(x + t0);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const double2 d = __ldg(p2 + j);
-                        mb = max(mb, (unsigned long long)__double_as_longlong(d.x) & 0x7FFFFFFFFFFFFFFFull);
-                        mb = max(mb, (unsigned long long)__double_as_longlong(d.y) & 0x7FFFFFFFFFFFFFFFull);
-                    }
-                } else {
-                    for (int j = 0; j < 16 && t0 + j < P.k; ++j) {
-                        const double d = __ldg(x + t0 + j);
-                        mb = max(mb, (unsigned long long)__double_as_longlong(d) & 0x7FFFFFFFFFFFFFFFull);
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-        if (kWarps > 1) {
-            if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = mb;
-            __syncthreads();
-            mb = 0;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) mb = max(mb, red[g * kWarps + w]);
-            __syncthreads();
-        }
-        (void)warp_in_group;
+        unsigned long long mb = live ? row_maxbits_part<GROUP, VEC>(x, P.k, gt) : 0ull;
+        mb = row_max_reduce<GROUP>(mb, g, red);
         if (!live) continue;
-
         const int e = exp_from_maxbits(mb);
         if (gt == 0) P.exps[row] = e;
-        const bool finite = e != kNonFiniteExp;
-        const int s = P.bits - e;
-        const double f1 = pow2(s >> 1), f2 = pow2(s - (s >> 1));
+        row_residues<GROUP, VEC>(P, x, row, e, gt);
+    }
+}
 
-        // Pass 2: the row again (from L1/L2), residues for every modulus.
-        int8_t* out_row = P.res + row * P.res_ld;
-        for (int64_t c = gt; c < nchunk_out; c += GROUP) {
-            const int64_t t0 = c * 16;
-            double v[16];
-            if (finite && VEC && t0 + 16 <= P.k) {
-                const double2* p2 = reinterpret_cast<const double2*>(x + t0);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const double2 d = __ldg(p2 + j);
-                    v[2 * j] = scale_round(d.x, f1, f2);
-                    v[2 * j + 1] = scale_round(d.y, f1, f2);
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    v[j] = (finite && t0 + j < P.k) ? scale_round(__ldg(x + t0 + j), f1, f2) : 0.0;
-            }
-            store_chunk_residues(v, P.n_mod, out_row + t0, P.res_plane);
-        }
+// The two passes as two kernels (FPEMU_SPLIT_ROWS=2): first every row's
+// exponent (one read of the operand at full bandwidth), ...
+template <int GROUP, bool VEC>
+__global__ void __launch_bounds__(256) split_rowexp_kernel(const __grid_constant__ SplitParams P) {
+    constexpr int kRowsPerCta = 256 / GROUP;
+    __shared__ unsigned long long red[256 / 32];
+    const int g = threadIdx.x / GROUP;
+    const int gt = threadIdx.x % GROUP;
+    for (int64_t row0 = (int64_t)blockIdx.x * kRowsPerCta; row0 < P.rows;
+         row0 += (int64_t)gridDim.x * kRowsPerCta) {
+        const int64_t row = row0 + g;
+        const bool live = row < P.rows;
+        unsigned long long mb = live ? row_maxbits_part<GROUP, VEC>(P.X + row * P.s_row, P.k, gt) : 0ull;
+        mb = row_max_reduce<GROUP>(mb, g, red);
+        if (live && gt == 0) P.exps[row] = exp_from_maxbits(mb);
+    }
+}
+
+// ... then the residues from the exponents (a second read of the operand).
+template <int GROUP, bool VEC>
+__global__ void __launch_bounds__(256) split_rowres_kernel(const __grid_constant__ SplitParams P) {
+    constexpr int kRowsPerCta = 256 / GROUP;
+    const int g = threadIdx.x / GROUP;
+    const int gt = threadIdx.x % GROUP;
+    for (int64_t row0 = (int64_t)blockIdx.x * kRowsPerCta; row0 < P.rows;
+         row0 += (int64_t)gridDim.x * kRowsPerCta) {
+        const int64_t row = row0 + g;
+        if (row < P.rows) row_residues<GROUP, VEC>(P, P.X + row * P.s_row, row, P.exps[row], gt);
     }
 }
 

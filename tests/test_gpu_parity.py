@@ -45,11 +45,15 @@ def _dtype(torch, g):
     return getattr(torch, g["dtype"].item().decode())
 
 
+@pytest.mark.parametrize("split_rows", ["1", "2"], ids=["one-kernel", "two-kernel"])
 @pytest.mark.parametrize("name", golden_names())
-def test_split_stage_matches_reference(torch_cuda, name):
+def test_split_stage_matches_reference(torch_cuda, name, split_rows, monkeypatch):
+    """Both forms of the K-contiguous split (FPEMU_SPLIT_ROWS: the row maximum and
+    the residues in one kernel, or in two) reproduce the reference's stages."""
     torch = torch_cuda
     from fp_emulation.ozaki import _split
 
+    monkeypatch.setenv("FPEMU_SPLIT_ROWS", split_rows)
     g = load_golden(name)
     bits, n_mod = int(g["bits"]), int(g["n_mod"])
     A, B = _cuda(torch, g["A"]), _cuda(torch, g["B"])
