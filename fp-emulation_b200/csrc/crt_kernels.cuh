@@ -41,35 +41,62 @@ __device__ __forceinline__ double crt_scale(double x, int re, int ce, int two_bi
     return ldexp(x, re + ce - two_bits);
 }
 
-// Standalone reconstruction from uint8 residues [n_mod][m][n] (the debug /
-// staged path; the fused GEMM epilogue uses the same three functions).
-// Each thread produces 4 consecutive columns of one row.
-__global__ void __launch_bounds__(256) crt_kernel(const uint8_t* __restrict__ res, int64_t m,
-                                                  int64_t n, int n_mod,
-                                                  const int32_t* __restrict__ row_exp,
-                                                  const int32_t* __restrict__ col_exp,
-                                                  int two_bits, double* __restrict__ C,
-                                                  int64_t ldc, const __grid_constant__ CrtConsts cc) {
-    const int64_t nq = (n + 3) / 4;
-    const int64_t plane = m * n;
-    for (int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; w < m * nq;
+// Standalone reconstruction from uint8 residues [n_mod][m][n] (the parity tap
+// of the reference's _reconstruct, and the second kernel of the split path).
+// A thread produces 16 consecutive columns of one row: 16-byte residue loads
+// per modulus when n is a multiple of 16, byte loads otherwise.  Output as in
+// the fused epilogue: double, or its float rounding, then the optional bias in
+// C's type, columns optionally scattered in segments (see GemmParams).
+__global__ void __launch_bounds__(256) crt_kernel(const __grid_constant__ CrtParams P) {
+    const int64_t nq = (P.n + 15) / 16;
+    const int64_t plane = P.m * P.n;
+    const bool vec = (P.n % 16) == 0 && (reinterpret_cast<uintptr_t>(P.res) % 16) == 0;
+    for (int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; w < P.m * nq;
          w += (int64_t)gridDim.x * blockDim.x) {
         const int64_t i = w / nq;
-        const int64_t j0 = (w % nq) * 4;
-        const int cnt = (int)min((int64_t)4, n - j0);
-        double hi[4] = {0.0, 0.0, 0.0, 0.0}, lo[4] = {0.0, 0.0, 0.0, 0.0};
-        const uint8_t* r = res + i * n + j0;
-        for (int l = 0; l < n_mod; ++l) {
-            const double wh = cc.wh[l], wm = cc.wm[l], wl = cc.wl[l];
+        const int64_t j0 = (w - i * nq) * 16;
+        const int cnt = (int)min((int64_t)16, P.n - j0);
+        double hi[16], lo[16];
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-                if (q < cnt) crt_step((double)r[(int64_t)l * plane + q], wh, wm, wl, hi[q], lo[q]);
+        for (int q = 0; q < 16; ++q) { hi[q] = 0.0; lo[q] = 0.0; }
+        const uint8_t* r = P.res + i * P.n + j0;
+#pragma unroll 1
+        for (int l = 0; l < P.n_mod; ++l) {
+            const double wh = P.cc.wh[l], wm = P.cc.wm[l], wl = P.cc.wl[l];
+            uint32_t b[4];
+            if (vec) {
+                const uint4 v = __ldcs(reinterpret_cast<const uint4*>(r + (int64_t)l * plane));
+                b[0] = v.x; b[1] = v.y; b[2] = v.z; b[3] = v.w;
+            } else {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint32_t x = 0;
+                    for (int e = 0; e < 4; ++e)
+                        if (4 * q + e < cnt) x |= (uint32_t)r[(int64_t)l * plane + 4 * q + e] << (8 * e);
+                    b[q] = x;
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+                crt_step((double)((b[q >> 2] >> (8 * (q & 3))) & 0xFFu), wh, wm, wl, hi[q], lo[q]);
         }
-        const int re = row_exp[i];
+        const int re = P.row_exp[i];
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-            if (q < cnt)
-                C[i * ldc + j0 + q] = crt_scale(crt_finish(hi[q], lo[q], cc), re, col_exp[j0 + q], two_bits);
+        for (int q = 0; q < 16; ++q) {
+            if (q < cnt) {
+                const int64_t j = j0 + q;
+                double v = crt_scale(crt_finish(hi[q], lo[q], P.cc), re, P.col_exp[j], P.two_bits);
+                const int64_t oc = P.col_seg > 0 ? (j / P.col_seg) * P.col_seg_stride + j % P.col_seg : j;
+                if (P.c_f32) {
+                    float f = __double2float_rn(v);
+                    if (P.bias) f = __fadd_rn(f, static_cast<const float*>(P.bias)[j]);
+                    static_cast<float*>(P.C)[i * P.ldc + oc] = f;
+                } else {
+                    if (P.bias) v = __dadd_rn(v, static_cast<const double*>(P.bias)[j]);
+                    static_cast<double*>(P.C)[i * P.ldc + oc] = v;
+                }
+            }
+        }
     }
 }
 

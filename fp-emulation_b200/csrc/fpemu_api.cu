@@ -286,17 +286,19 @@ int max_active_units(const DevInfo& d) {
 // 64 tiles take 64 pairs rather than 74 (no slower: every unit does one tile per
 // pass either way) and leave SMs free for kernels on other streams.
 template <class Cfg>
-int gemm_units(const DevInfo& d, int64_t m, int64_t n) {
+int gemm_cap(const DevInfo& d) {
     static std::mutex mu;
     static int cache[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    int cap;
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        if (cache[dev & 63] == 0) cache[dev & 63] = max_active_units<Cfg, kModeCrt>(d);
-        cap = cache[dev & 63];
-    }
+    std::lock_guard<std::mutex> lk(mu);
+    if (cache[dev & 63] == 0) cache[dev & 63] = max_active_units<Cfg, kModeCrt>(d);
+    return cache[dev & 63];
+}
+
+template <class Cfg>
+int gemm_units(const DevInfo& d, int64_t m, int64_t n) {
+    const int cap = gemm_cap<Cfg>(d);
     const int64_t tiles = ((m + Cfg::kTileM - 1) / Cfg::kTileM) * ((n + Cfg::BN - 1) / Cfg::BN);
     if (cap <= 0 || tiles <= 0) return 0;
     const int64_t waves = (tiles + cap - 1) / cap;
@@ -329,6 +331,28 @@ int gemm_sched() {
     return (s && strcmp(s, "tile") == 0) ? kSchedTileMajor : kSchedModulusMajor;
 }
 
+// Which form the fused GEMM + CRT stage takes for an m x n product:
+//   0, fused: one kernel -- per-modulus GEMMs, mod and the CRT in the epilogue;
+//   1, split: the residue GEMM with every (tile, modulus) unit dealt out to all
+//      CTA pairs (kSchedSpread), the residues to the workspace, then the CRT
+//      kernel over every SM.  When a product has few tiles per CTA pair, the
+//      fused kernel leaves pairs idle and runs each tile's moduli and FP64 CRT
+//      on one pair; the split form spreads both over the device.
+// Auto: split when the product has fewer than kSplitTilesPerUnit tiles per CTA
+// pair the device holds.  FPEMU_GEMM_PATH=fused|split forces one.
+constexpr int kSplitTilesPerUnit = 4;
+
+int gemm_path(const DevInfo& d, int64_t m, int64_t n) {
+    const char* s = getenv("FPEMU_GEMM_PATH");
+    if (s && strcmp(s, "fused") == 0) return 0;
+    if (s && strcmp(s, "split") == 0) return 1;
+    const bool pairs = use_pairs();
+    const int64_t tm = pairs ? MainCfg::kTileM : SingleCfg::kTileM;
+    const int64_t tiles = ((m + tm - 1) / tm) * ((n + MainCfg::BN - 1) / MainCfg::BN);
+    const int cap = pairs ? gemm_cap<MainCfg>(d) : gemm_cap<SingleCfg>(d);
+    return (cap > 0 && tiles < (int64_t)kSplitTilesPerUnit * cap) ? 1 : 0;
+}
+
 template <class Cfg>
 int64_t staging_slots(const DevInfo& d, int64_t m, int64_t n, int sched) {
     if (sched == kSchedTileMajor) return (int64_t)gemm_units<Cfg>(d, m, n) * Cfg::CG;  // one per CTA
@@ -340,6 +364,7 @@ int64_t staging_slots(const DevInfo& d, int64_t m, int64_t n, int sched) {
 // slots are the same size: one CTA's 128 x 256 share of a tile).
 size_t gemm_scratch_bytes(const DevInfo& d, int64_t m, int64_t n, int n_mod, int sched) {
     static_assert(MainCfg::kBRows * MainCfg::CG == SingleCfg::BN, "slot sizes agree");
+    if (gemm_path(d, m, n) == 1) return align256((size_t)n_mod * (size_t)m * (size_t)n) + 256;  // residues
     const int64_t slots = std::max(staging_slots<MainCfg>(d, m, n, sched), staging_slots<SingleCfg>(d, m, n, sched));
     // Plus the per-pass counters of the modulus-major schedule, after the slots.
     return align256((size_t)slots * (size_t)MainCfg::slot_bytes(n_mod)) + 256;
@@ -434,6 +459,8 @@ int launch_gemm_cfg(GemmParams& P, const int8_t* a_res, const int8_t* b_res, int
     P.test_stall_idx = test_stall_idx();
     mod_consts(P.n_mod, &P.mc);
     int units = gemm_units<Cfg>(d, m, n);
+    if (P.sched == kSchedSpread)  // every unit the device holds, up to one per (tile, modulus)
+        units = (int)std::min<int64_t>(gemm_cap<Cfg>(d), (int64_t)P.num_tiles * P.n_mod);
     if (max_ctas > 0 && units > max_ctas / Cfg::CG) units = max_ctas / Cfg::CG;
     if (units < 1) return fail(FPEMU_ERR_CUDA, "GEMM kernel cannot be made resident on this device");
     auto kern = ozaki_gemm_kernel<Cfg, MODE>;
@@ -540,6 +567,19 @@ int check_gemm_args(int64_t m, int64_t n, int64_t k, int n_mod, const void* a_re
     if ((m > 0 && n > 0) && (a_res == nullptr || b_res == nullptr)) return fail(FPEMU_ERR_INVALID, "null residue pointer");
     if ((reinterpret_cast<uintptr_t>(a_res) | reinterpret_cast<uintptr_t>(b_res)) % 16 != 0)
         return fail(FPEMU_ERR_INVALID, "residue buffers must be 16-byte aligned");
+    return FPEMU_OK;
+}
+
+// The standalone CRT kernel over the whole device (or max_ctas CTAs).
+int launch_crt(const CrtParams& P, const DevInfo& d, cudaStream_t st, int max_ctas) {
+    const int64_t work = P.m * ((P.n + 15) / 16);
+    int64_t grid = (work + 255) / 256;
+    int64_t cap = (int64_t)d.sms * 8;
+    if (max_ctas > 0 && cap > max_ctas) cap = max_ctas;
+    if (grid > cap) grid = cap;
+    if (grid < 1) return FPEMU_OK;
+    crt_kernel<<<(unsigned)grid, 256, 0, st>>>(P);
+    FPEMU_CUDA(cudaGetLastError());
     return FPEMU_OK;
 }
 
@@ -676,13 +716,19 @@ int fpemu_crt_reconstruct(int64_t m, int64_t n, int n_mod, const uint8_t* res, c
     if (!res || !row_exp || !col_exp || !C) return fail(FPEMU_ERR_INVALID, "crt: null pointer");
     CrtConsts cc;
     FPEMU_TRY(crt_weights(n_mod, &cc));
-    const int64_t work = m * ((n + 3) / 4);
-    int64_t grid = (work + 255) / 256;
-    if (grid > (int64_t)d.sms * 32) grid = (int64_t)d.sms * 32;
-    crt_kernel<<<(unsigned)grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(res, m, n, n_mod, row_exp, col_exp,
-                                                                           2 * bits, C, ldc, cc);
-    FPEMU_CUDA(cudaGetLastError());
-    return FPEMU_OK;
+    CrtParams P;
+    memset(&P, 0, sizeof P);
+    P.res = res;
+    P.m = m;
+    P.n = n;
+    P.n_mod = n_mod;
+    P.row_exp = row_exp;
+    P.col_exp = col_exp;
+    P.two_bits = 2 * bits;
+    P.C = C;
+    P.ldc = ldc;
+    P.cc = cc;
+    return launch_crt(P, d, static_cast<cudaStream_t>(stream), 0);
 }
 
 int fpemu_gemm_crt(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_res, const int8_t* b_res,
@@ -737,6 +783,36 @@ int gemm_crt_impl(int64_t m, int64_t n, int64_t k, int n_mod, const int8_t* a_re
     if (workspace == nullptr || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
         return fail(FPEMU_ERR_WORKSPACE, "gemm_crt: need %zu bytes of 256-byte aligned workspace, got %zu",
                     need, workspace_bytes);
+    if (gemm_path(d, m, n) == 1) {
+        // Split form: spread residue GEMM into the workspace, then the CRT kernel.
+        GemmParams G;
+        memset(&G, 0, sizeof G);
+        G.m = (int)m;
+        G.n = (int)n;
+        G.k = (int)k;
+        G.n_mod = n_mod;
+        G.out = workspace;
+        G.sched = kSchedSpread;
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        FPEMU_TRY(launch_gemm<kModeResidue>(G, a_res, b_res, res_ld, b_res_plane, d, st, max_ctas));
+        CrtParams Q;
+        memset(&Q, 0, sizeof Q);
+        Q.res = static_cast<const uint8_t*>(workspace);
+        Q.m = m;
+        Q.n = n;
+        Q.n_mod = n_mod;
+        Q.row_exp = row_exp;
+        Q.col_exp = col_exp;
+        Q.two_bits = 2 * bits;
+        Q.C = C;
+        Q.ldc = ldc;
+        Q.c_f32 = c_dtype == FPEMU_C_F32;
+        Q.bias = bias;
+        Q.col_seg = col_seg;
+        Q.col_seg_stride = col_seg_stride;
+        FPEMU_TRY(crt_weights(n_mod, &Q.cc));
+        return launch_crt(Q, d, st, max_ctas);
+    }
     GemmParams P;
     memset(&P, 0, sizeof P);
     P.m = (int)m;

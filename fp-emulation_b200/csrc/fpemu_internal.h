@@ -34,6 +34,24 @@ struct CrtConsts {
     double M_hi, M_lo, inv_M;
 };
 
+// The standalone CRT kernel: C from uint8 residues [n_mod][m][n], with the
+// output options of the fused epilogue (float32 cast, bias, column segments).
+struct CrtParams {
+    const uint8_t* res;
+    int64_t m, n;
+    int n_mod;
+    const int32_t* row_exp;
+    const int32_t* col_exp;
+    int two_bits;
+    void* C;
+    int64_t ldc;
+    int c_f32;
+    const void* bias;
+    int col_seg;
+    int64_t col_seg_stride;
+    CrtConsts cc;
+};
+
 struct SplitParams {
     const double* X;
     int64_t rows, k, s_row, s_k;
@@ -55,7 +73,11 @@ enum GemmMode : int { kModeRaw = 0, kModeResidue = 1, kModeCrt = 2 };
 //   kSchedTileMajor: all moduli of a tile back to back; staging is one reusable
 //     slot per CTA (bounded workspace), at the cost of re-reading A and B strips
 //     from DRAM for every modulus.
-enum GemmSched : int { kSchedModulusMajor = 0, kSchedTileMajor = 1 };
+//   kSchedSpread (mode 1 only, the split path): the (tile, modulus) units of the
+//     whole product are dealt out round-robin in modulus-major order to every
+//     CTA (pair), so a product with fewer tiles than CTAs still uses them all;
+//     the residues go to global memory and a separate kernel runs the CRT.
+enum GemmSched : int { kSchedModulusMajor = 0, kSchedTileMajor = 1, kSchedSpread = 2 };
 
 // Index of the "stop aligning" flag in the 64 pass counters of the modulus-major
 // schedule (passes use [0, n_mod), n_mod <= 25).

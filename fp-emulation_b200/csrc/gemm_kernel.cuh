@@ -176,11 +176,19 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     // MMA time in FP64 work) alternates with a light epilogue (a) instead of
     // all CRTs queueing behind the last pass's MMAs.  (i,a) still precedes
     // (i,b), whose CRT reads the plane staged at (i,a).
+    const bool spread = P.sched == kSchedSpread;
     const int my_tiles = (P.num_tiles - unit + num_units - 1) / num_units;
-    const int my_units = my_tiles * P.n_mod;
+    const int my_units = spread ? (int)(((int64_t)P.num_tiles * P.n_mod - unit + num_units - 1) / num_units)
+                                : my_tiles * P.n_mod;
     const bool tail = P.sched != kSchedTileMajor && P.tail && P.n_mod >= 2;
     const int tail_base = (P.n_mod - 2) * my_tiles;
     auto unit_at = [&](int idx, int& tile, int& l) {
+        if (spread) {  // global unit u = l * num_tiles + tile, dealt out round-robin
+            const int64_t u = (int64_t)idx * num_units + unit;
+            l = (int)(u / P.num_tiles);
+            tile = (int)(u - (int64_t)l * P.num_tiles);
+            return;
+        }
         int i;
         if (P.sched == kSchedTileMajor) {
             i = idx / P.n_mod;

@@ -19,6 +19,15 @@ from oracle import ozaki_oracle as oo
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(params=["fused", "split"], autouse=True)
+def gemm_path(request, monkeypatch):
+    """Every test of this module runs on both forms of the GEMM + CRT stage: the
+    fused kernel and the split form (spread residue GEMM, then the CRT kernel);
+    FPEMU_GEMM_PATH forces one where the size would pick the other."""
+    monkeypatch.setenv("FPEMU_GEMM_PATH", request.param)
+    return request.param
+
+
 @pytest.fixture(scope="module")
 def torch_cuda():
     import torch

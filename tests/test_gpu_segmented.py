@@ -16,9 +16,11 @@ from oracle import ozaki_oracle as oo
 pytestmark = pytest.mark.gpu
 
 
-def test_segmented_columns_land_in_their_blocks():
+@pytest.mark.parametrize("path", ["fused", "split"])
+def test_segmented_columns_land_in_their_blocks(path, monkeypatch):
     import torch
 
+    monkeypatch.setenv("FPEMU_GEMM_PATH", path)
     from fp_emulation import _lib
     from fp_emulation.ozaki import _n_moduli, _res_ld, _split
 
