@@ -2,7 +2,7 @@
 // from its residues, in the reference's floating-point operation order
 // (crt_reconstruct.cpp:13-37 / crt_kernel.cu:105-127 of thezettascale/fp-emulation):
 // double-double accumulation of r_l * (wh_l + wm_l + wl_l) with TwoProduct and
-// TwoSum, q = rint(acc * inv_M), acc - q*M in double-double, then ldexp.
+// an exact two-sum, q = rint(acc * inv_M), acc - q*M in double-double, then ldexp.
 //
 // Every operation is an explicit round-to-nearest intrinsic so the compiler
 // cannot fuse a multiply into a neighbouring add; the only FMAs are the ones
@@ -15,13 +15,25 @@
 namespace fpemu {
 
 // One accumulation step for residue r (crt_reconstruct.cpp:17-26).
+//
+// The reference takes the rounding error t of s = hi + p with TwoSum (six
+// operations).  Here both addends are non-negative -- residues and CRT weights
+// are, so every p and every partial sum hi is -- hence their order by magnitude
+// is the order of their bit patterns, picked with integer compares, and Fast2Sum
+// on (larger, smaller) gives the same exact error in two operations (Dekker:
+// for |a| >= |b|, s - a and b - (s - a) are exact).  Both forms yield the exact
+// value of (hi + p) - s, a representable double, so t and everything after it
+// are bit-identical to the reference's.
 __device__ __forceinline__ void crt_step(double r, double wh, double wm, double wl, double& hi,
                                          double& lo) {
     const double p = __dmul_rn(r, wh);
     const double e = __fma_rn(r, wh, -p);
     const double s = __dadd_rn(hi, p);
-    const double v = __dsub_rn(s, hi);
-    const double t = __dadd_rn(__dsub_rn(hi, __dsub_rn(s, v)), __dsub_rn(p, v));
+    const unsigned long long hb = (unsigned long long)__double_as_longlong(hi);
+    const unsigned long long pb = (unsigned long long)__double_as_longlong(p);
+    const double big = __longlong_as_double((long long)(hb > pb ? hb : pb));
+    const double small = __longlong_as_double((long long)(hb > pb ? pb : hb));
+    const double t = __dsub_rn(small, __dsub_rn(s, big));
     hi = s;
     lo = __dadd_rn(__dadd_rn(__dadd_rn(lo, __fma_rn(r, wm, e)), __dmul_rn(r, wl)), t);
 }
