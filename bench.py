@@ -396,17 +396,22 @@ def run_ours(args):
         peak, peak_src = 2.0 * 1590.0, "2 x 1.59 PFLOP/s burst bf16 of fallback"
         peak_sus = 2.0 * 1400.0
     # Our kernels per step and rank.  One GPU: split A, split B (column max +
-    # split), the fused GEMM.  Root-split transports (ce, nccl): split A, split B
-    # per chunk on the root (2 kernels), one GEMM per chunk.  Ring: split A, and per
-    # chunk the strip's 2 split kernels and one GEMM.
+    # split), the GEMM stage (1 kernel fused, 2 in the split form).  Root-split
+    # transports (ce, nccl): split A, split B per chunk on the root (2 kernels), the
+    # GEMM stage per chunk.  Rings: split A, and per chunk the strip's 2 split
+    # kernels and the GEMM stage.
     if world == 1:
-        per_rank = 4
-    elif sharded:
-        per_rank = 1 + 3 * len(fdist.plan_column_chunks(nb, fdist.allgather_strip_cols(world)))
-    elif transport_used == "ce-ring":
-        per_rank = 1 + 3 * n_chunks
+        per_rank = 3 + lib.fpemu_gemm_kernels(m, n)
     else:
-        per_rank = 1 + n_chunks + (2 * n_chunks if rank == root else 0)
+        cw = [c1 - c0 for c0, c1 in fdist.plan_column_chunks(n)]
+        if sharded:
+            sw = fdist.allgather_strip_cols(world)
+            cw = [world * min(sw, nb - c0) for c0 in range(0, nb, sw)]
+        gk = sum(lib.fpemu_gemm_kernels(m, w) for w in cw)
+        if sharded or transport_used == "ce-ring":
+            per_rank = 1 + 2 * len(cw) + gk
+        else:
+            per_rank = 1 + gk + (2 * len(cw) if rank == root else 0)
     launches = int(sum_over_ranks(per_rank * args.steps))
 
     # ---- end to end through the public op, host buffers ------------------

@@ -649,6 +649,13 @@ size_t fpemu_gemm_workspace_size(int64_t m, int64_t n, int n_mod) {
     return gemm_scratch_bytes(d, m, n, n_mod, gemm_sched());
 }
 
+int fpemu_gemm_kernels(int64_t m, int64_t n) {
+    DevInfo d;
+    if (device_info(&d) != FPEMU_OK || m < 0 || n < 0) return 0;
+    if (m == 0 || n == 0) return 0;
+    return gemm_path(d, m, n) == 1 ? 2 : 1;
+}
+
 size_t fpemu_workspace_size(int64_t m, int64_t n, int64_t k, int n_mod) {
     DevInfo d;
     if (device_info(&d) != FPEMU_OK || m < 0 || n < 0 || k < 1 || n_mod < 1 || n_mod > kMaxModuli) return 0;

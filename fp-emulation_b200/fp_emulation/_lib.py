@@ -44,6 +44,7 @@ SIGNATURES = {
     "fpemu_gemm_crt": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _i64, _vp, _vp, _int, _vp, _i64,
                               _int, _vp, _sz, _vp]),
     "fpemu_gemm_workspace_size": (_sz, [_i64, _i64, _int]),
+    "fpemu_gemm_kernels": (_int, [_i64, _i64]),
     "fpemu_ozaki2_gemm_ex": (_int, [_i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _int, _vp,
                                     _int, _int, _vp, _sz, _vp]),
     "fpemu_gemm_crt_ex": (_int, [_i64, _i64, _i64, _int, _vp, _vp, _i64, _i64, _vp, _vp, _int, _vp, _i64,

@@ -183,8 +183,15 @@ int fpemu_gemm_crt_noalloc(int64_t m, int64_t n, int64_t k, int n_mod, const int
                            const int32_t *col_exp, int bits, double *C, int64_t ldc,
                            void *stream);
 
+/* Kernels one fpemu_gemm_crt / _ex / _segmented call launches for an m x n
+ * product on the current device: 1 (the fused GEMM + CRT kernel) or 2 (the
+ * split form for products with few tiles per CTA pair: the residue GEMM, then
+ * the CRT kernel; FPEMU_GEMM_PATH forces one).  0 on error.  No counterpart in
+ * the reference. */
+int fpemu_gemm_kernels(int64_t m, int64_t n);
+
 /* Workspace bytes fpemu_gemm_crt / fpemu_gemm_residues need (the epilogue's
- * per-CTA residue staging). */
+ * per-CTA residue staging, or the split form's residues). */
 size_t fpemu_gemm_workspace_size(int64_t m, int64_t n, int n_mod);
 
 /* ---- device status ---------------------------------------------------------- */
