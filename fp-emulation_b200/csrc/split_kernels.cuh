@@ -307,16 +307,22 @@ __global__ void __launch_bounds__(256) split_strided_kernel(const __grid_constan
     const int64_t k0 = (int64_t)blockIdx.y * kTileK;
 
     // Load: thread (tr = tid % 32, tk = tid / 32) reads rows r0+tr, k = k0+tk+8i.
+    // All 16 loads are issued before the first shared-memory store, so a CTA
+    // keeps its whole 32 KB tile in flight.
     {
         const int tr = threadIdx.x % kTileR;
         const int tk = threadIdx.x / kTileR;
         const int64_t r = r0 + tr;
-#pragma unroll 4
+        double v[kTileK / 8];
+#pragma unroll
         for (int i = 0; i < kTileK / 8; ++i) {
             const int64_t t = k0 + tk + 8 * i;
+            v[i] = (r < P.rows && t < P.k) ? __ldg(P.X + r * P.s_row + t * P.s_k) : 0.0;
+        }
+#pragma unroll
+        for (int i = 0; i < kTileK / 8; ++i) {
             const int lt = tk + 8 * i;
-            tile[lt][tr ^ (((lt >> 4) & 7) << 2)] =
-                (r < P.rows && t < P.k) ? __ldg(P.X + r * P.s_row + t * P.s_k) : 0.0;
+            tile[lt][tr ^ (((lt >> 4) & 7) << 2)] = v[i];
         }
     }
     __syncthreads();
