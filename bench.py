@@ -934,29 +934,55 @@ def dt_pinn_step(torch, dev, args, n_steps=20):
     ops_fp64 = (DX, DT, DXX)
     ops_oz = tuple(prepare_operand(M, "left") for M in ops_fp64)
 
-    def make(emulated):
+    # Index tensors instead of boolean masks: a mask index waits for the host to
+    # learn its size, which also rules out CUDA-graph capture.
+    ic_idx, bc_idx = ic.nonzero().squeeze(1), bc.nonzero().squeeze(1)
+    ic_x = torch.sin(torch.pi * X.index_select(0, ic_idx)[:, 0:1])
+
+    def make(emulated, capturable=False):
         model = convert(net()) if emulated else net()
-        opt = torch.optim.Adam(model.parameters(), lr=1e-3)
+        opt = torch.optim.Adam(model.parameters(), lr=1e-3, capturable=capturable)
         mm = ozaki2_int8_matmul if emulated else torch.matmul
         ops = ops_oz if emulated else ops_fp64
 
         def step():
             u = model(X)
             u_x, u_t, u_xx = mm(ops[0], u), mm(ops[1], u), mm(ops[2], u)
-            loss = (u_t + u * u_x - nu * u_xx).pow(2).mean() + 10 * (u[ic] + torch.sin(torch.pi * X[ic, 0:1])).pow(
-                2).mean() + 10 * u[bc].pow(2).mean()
-            opt.zero_grad()
+            loss = (u_t + u * u_x - nu * u_xx).pow(2).mean() + \
+                10 * (u.index_select(0, ic_idx) + ic_x).pow(2).mean() + 10 * u.index_select(0, bc_idx).pow(2).mean()
+            opt.zero_grad(set_to_none=False)
             loss.backward()
             opt.step()
             return loss
 
         return step
 
+    def graphed(emulated):
+        """The same step captured once in a CUDA graph and replayed: the
+        launch-bound inner loop without host work between the kernels."""
+        step = make(emulated, capturable=True)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):  # warm-up on the capturing stream: optimizer state, caches
+                step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        return g.replay
+
     ms_oz = _time(torch, dev, make(True), n_steps, 3)
     ms_fp = _time(torch, dev, make(False), n_steps, 3)
-    return {"grid": f"{Nx + 1} x {Nt + 1} Chebyshev points, operators {tuple(DX.shape)}",
-            "ms_emulated": round(ms_oz, 3), "ms_native_fp64": round(ms_fp, 3),
-            "what": "forward + backward + Adam step; emulated: convert()'ed network and prepared DX, DT, DXX"}
+    out = {"grid": f"{Nx + 1} x {Nt + 1} Chebyshev points, operators {tuple(DX.shape)}",
+           "ms_emulated": round(ms_oz, 3), "ms_native_fp64": round(ms_fp, 3),
+           "what": "forward + backward + Adam step; emulated: convert()'ed network and prepared DX, DT, DXX"}
+    try:
+        out["ms_emulated_cuda_graph"] = round(_time(torch, dev, graphed(True), n_steps, 3), 3)
+        out["ms_native_fp64_cuda_graph"] = round(_time(torch, dev, graphed(False), n_steps, 3), 3)
+    except Exception as exc:  # a capture the runtime refuses is reported, not fatal
+        out["cuda_graph_error"] = str(exc)[:300]
+    return out
 
 
 # ---------------------------------------------------------------- reference arm ---
