@@ -1,5 +1,6 @@
-"""The column-sharded multi-GPU product (distributed.rowsharded_product_allgather)
-end to end on CPU ranks: gloo process groups, a fake CUDA runtime that really
+"""The multi-GPU products of fp_emulation.distributed end to end on CPU ranks --
+the column-sharded product (rowsharded_product_allgather) and the root-held
+products over the copy-engine ring and chain: gloo process groups, a fake CUDA runtime that really
 moves the bytes -- each rank's transport buffer is a shared-memory block that
 the peers map in place of CUDA IPC, every copy the ring enqueues is done at once
 -- and a CPU backend whose split and segmented GEMM + CRT come from the oracle.
@@ -15,6 +16,7 @@ product, for 2 and 3 ranks, two calls in a row, and a ragged last chunk.
 from __future__ import annotations
 
 import contextlib
+import ctypes
 import os
 import socket
 import traceback
@@ -30,7 +32,14 @@ from cuda.bindings import runtime as _real_rt
 from oracle import ozaki_oracle as oo
 
 OK = _real_rt.cudaError_t.cudaSuccess
-SPAN = 0x10000000  # fake device addresses: rank r's buffer at (r + 1) * SPAN
+# Fake device addresses: rank r's buffer at BASE + r * SPAN, far from where a
+# process maps its own memory (the ring also copies from the root's host B).
+BASE = 0x100000000000
+SPAN = 0x10000000
+
+
+def _fake_base(r):
+    return BASE + r * SPAN
 
 
 def _free_port():
@@ -63,7 +72,7 @@ class MemRt:
 
     def cudaMalloc(self, nbytes):
         shm = shared_memory.SharedMemory(create=True, size=nbytes, name=f"{self.tag}_{self.rank}")
-        base = SPAN * (self.rank + 1)
+        base = _fake_base(self.rank)
         self.shm[base] = shm
         return OK, base
 
@@ -72,13 +81,16 @@ class MemRt:
 
     def cudaIpcOpenMemHandle(self, h, flags):
         name, r = h.reserved.decode().split("|")
-        base = SPAN * (int(r) + 1)
+        base = _fake_base(int(r))
         self.shm[base] = shared_memory.SharedMemory(name=name)
         return OK, base
 
     def _view(self, addr, n):
-        base = addr - addr % SPAN
-        return np.frombuffer(self.shm[base].buf, dtype=np.uint8, count=n, offset=addr - base)
+        for base, shm in self.shm.items():
+            if base <= addr and addr + n <= base + shm.size:
+                return np.frombuffer(shm.buf, dtype=np.uint8, count=n, offset=addr - base)
+        # Any other address is host memory of this process (the root's B, staged by the ring).
+        return np.ctypeslib.as_array((ctypes.c_uint8 * n).from_address(addr))
 
     def cudaMemcpyAsync(self, dst, src, nbytes, kind, stream):
         self._view(dst, nbytes)[:] = self._view(src, nbytes)
@@ -148,6 +160,9 @@ class OracleOps:
         res[:, :, :k] = torch.from_numpy(oo.residues(A_int, oo.PRIMES[:n_mod]))
         exps.copy_(torch.from_numpy(re))
 
+    def gemm_crt(self, a_res, re, b_res, ce_chunk, bits, C, c0, c1, k):
+        self.gemm_crt_segmented(a_res, re, b_res, ce_chunk, bits, C, c0, c1 - c0, c1 - c0, k)
+
     def gemm_crt_segmented(self, a_res, re, b_res, ce_chunk, bits, C, col_off, seg, seg_stride, k):
         n_mod = a_res.shape[0]
         moduli = oo.PRIMES[:n_mod]
@@ -164,7 +179,7 @@ def _problem(m, k, n):
     return A, B
 
 
-def _worker(rank, world, port, m, k, nb, strip, q):
+def _worker(rank, world, port, m, k, nb, strip, q, transport="allgather"):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         import torch.distributed as dist
@@ -194,7 +209,16 @@ def _worker(rank, world, port, m, k, nb, strip, q):
             def _current_stream(self):
                 return _Stream()
 
+        class MemChain(ct.CeChain):
+            _rt = rt
+            _device_ctx = MemRing._device_ctx
+            _wrap_buffer = MemRing._wrap_buffer
+            _local_event = MemRing._local_event
+            _new_stream = MemRing._new_stream
+            _current_stream = MemRing._current_stream
+
         ct.CeRing = MemRing
+        ct.TRANSPORTS = {"ce": MemChain, "ce-ring": MemRing}
         torch.cuda.current_stream = lambda device=None: _Stream()
         torch.cuda.stream = lambda s: contextlib.nullcontext()
         torch.Tensor.record_stream = lambda self, s: None
@@ -204,13 +228,23 @@ def _worker(rank, world, port, m, k, nb, strip, q):
         A_local = torch.from_numpy(A[r0:r1])
         B_local = torch.from_numpy(np.ascontiguousarray(B[:, rank * nb:(rank + 1) * nb]))
         n_mod = oo.n_moduli(k, 53)
-        outs = [fd.rowsharded_product_allgather(A_local, B_local, k, 53, n_mod, OracleOps(), strip_cols=strip)
-                .numpy().copy() for _ in range(2)]
+        B_root = torch.from_numpy(B) if rank == 0 else None
+        n = world * nb
+
+        def product():
+            if transport == "allgather":
+                return fd.rowsharded_product_allgather(A_local, B_local, k, 53, n_mod, OracleOps(), strip_cols=strip)
+            if transport == "ce-ring":
+                return fd.rowsharded_product_ring(A_local, B_root, n, k, 53, n_mod, OracleOps(), chunk_cols=strip)
+            return fd.rowsharded_product_ce(A_local, B_root, n, k, 53, n_mod, OracleOps(), chunk_cols=strip,
+                                            transport="ce")
+
+        outs = [product().numpy().copy() for _ in range(2)]
         q.put((rank, "ok", (r0, r1, outs)))
         dist.barrier()
         for shm in rt.shm.values():
             shm.close()
-        own = rt.shm.get(SPAN * (rank + 1))
+        own = rt.shm.get(_fake_base(rank))
         if own is not None:
             own.unlink()
         dist.destroy_process_group()
@@ -218,13 +252,20 @@ def _worker(rank, world, port, m, k, nb, strip, q):
         q.put((rank, "error", traceback.format_exc()))
 
 
-@pytest.mark.parametrize("world,nb,strip", [(2, 50, 16), (3, 33, 16)])
-def test_allgather_product_on_cpu_ranks_matches_the_oracle(world, nb, strip):
+@pytest.mark.parametrize("transport,world,nb,strip", [("allgather", 2, 50, 16), ("allgather", 3, 33, 16),
+                                                     ("ce-ring", 2, 50, 256), ("ce-ring", 3, 100, 256),
+                                                     ("ce", 3, 100, 256)])
+def test_multi_gpu_products_on_cpu_ranks_match_the_oracle(transport, world, nb, strip):
+    """allgather: column-sharded B (strips of `strip` columns).  ce-ring and ce: B on
+    rank 0, chunks of `strip` columns (the ring stages FP64 strips from the root's
+    B, splits them on every rank and circulates the residues; the chain has the
+    root split every chunk and relays it in pieces)."""
     m, k = 80, 70
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, m, k, nb, strip, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, m, k, nb, strip, q, transport))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=180) for _ in range(world)]
