@@ -58,7 +58,9 @@ __device__ __forceinline__ double crt_scale(double x, int re, int ce, int two_bi
 // A thread produces 16 consecutive columns of one row: 16-byte residue loads
 // per modulus when n is a multiple of 16, byte loads otherwise.  Output as in
 // the fused epilogue: double, or its float rounding, then the optional bias in
-// C's type, columns optionally scattered in segments (see GemmParams).
+// C's type, columns optionally scattered in segments (see GemmParams).  An
+// output with a residue byte >= 128 -- never a residue (p <= 127); the residue
+// GEMM writes 0xFF over units it could not finish -- becomes NaN.
 __global__ void __launch_bounds__(256) crt_kernel(const __grid_constant__ CrtParams P) {
     const int64_t nq = (P.n + 15) / 16;
     const int64_t plane = P.m * P.n;
@@ -71,6 +73,7 @@ __global__ void __launch_bounds__(256) crt_kernel(const __grid_constant__ CrtPar
         double hi[16], lo[16];
 #pragma unroll
         for (int q = 0; q < 16; ++q) { hi[q] = 0.0; lo[q] = 0.0; }
+        uint32_t seen[4] = {0u, 0u, 0u, 0u};  // OR of every modulus's bytes: bit 7 marks a non-residue
         const uint8_t* r = P.res + i * P.n + j0;
 #pragma unroll 1
         for (int l = 0; l < P.n_mod; ++l) {
@@ -89,6 +92,8 @@ __global__ void __launch_bounds__(256) crt_kernel(const __grid_constant__ CrtPar
                 }
             }
 #pragma unroll
+            for (int q = 0; q < 4; ++q) seen[q] |= b[q];
+#pragma unroll
             for (int q = 0; q < 16; ++q)
                 crt_step((double)((b[q >> 2] >> (8 * (q & 3))) & 0xFFu), wh, wm, wl, hi[q], lo[q]);
         }
@@ -98,6 +103,7 @@ __global__ void __launch_bounds__(256) crt_kernel(const __grid_constant__ CrtPar
             if (q < cnt) {
                 const int64_t j = j0 + q;
                 double v = crt_scale(crt_finish(hi[q], lo[q], P.cc), re, P.col_exp[j], P.two_bits);
+                if ((seen[q >> 2] >> (8 * (q & 3))) & 0x80u) v = __longlong_as_double(0x7FF8000000000000ll);
                 const int64_t oc = P.col_seg > 0 ? (j / P.col_seg) * P.col_seg_stride + j % P.col_seg : j;
                 if (P.c_f32) {
                     float f = __double2float_rn(v);

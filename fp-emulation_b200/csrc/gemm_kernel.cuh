@@ -448,6 +448,23 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 }
             }
         }
+        if (MODE == kModeResidue && idx < my_units) {
+            // Aborted at unit idx: mark this thread's part of every unit it did not
+            // write with 0xFF, which no residue can be (p <= 127); the CRT kernel
+            // turns an output with such a residue into NaN.
+#pragma unroll 1
+            for (int j = idx; j < my_units; ++j) {
+                int tile, l, tm, tn;
+                unit_at(j, tile, l);
+                tile_coords(tile, P.tiles_m, P.tiles_n, P.band_rows, tm, tn);
+                const int64_t row = (int64_t)tm * Cfg::kTileM + row_in_tile;
+                if (row >= P.m) continue;
+                const int col0 = tn * BN + cg * Cfg::kCols;
+                uint8_t* o = static_cast<uint8_t*>(P.out) + ((int64_t)l * P.m + row) * P.n;
+#pragma unroll 1
+                for (int c = 0; c < Cfg::kCols && col0 + c < P.n; ++c) o[col0 + c] = 0xFFu;
+            }
+        }
         if (MODE == kModeCrt && idx < my_units) {
             // Aborted at unit idx: every tile whose last modulus comes at or after
             // idx was not reconstructed.  Mark this thread's part of them NaN.
