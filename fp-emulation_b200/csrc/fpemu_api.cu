@@ -339,8 +339,13 @@ int gemm_sched() {
 //      fused kernel leaves pairs idle and runs each tile's moduli and FP64 CRT
 //      on one pair; the split form spreads both over the device.
 // Auto: split when the product has fewer than kSplitTilesPerUnit tiles per CTA
-// pair the device holds.  FPEMU_GEMM_PATH=fused|split forces one.
-constexpr int kSplitTilesPerUnit = 4;
+// pair the device holds.  FPEMU_GEMM_PATH=fused|split forces one.  Measured on
+// B200 (same inputs, identical results): the split form takes 0.27x the fused
+// time at n = 1024, 0.78x at 2048 and 4096, 0.93x at 8192 (14 tiles per pair),
+// 0.92-0.94x on the multi-GPU chunk shapes (2048-16384 x 2048 x 8192-16384),
+// but 1.18x at n = 16384 (55 tiles per pair), where its CTA pairs, which do not
+// align their modulus passes, drift apart and lose the L2 reuse.
+constexpr int kSplitTilesPerUnit = 28;
 
 int gemm_path(const DevInfo& d, int64_t m, int64_t n) {
     const char* s = getenv("FPEMU_GEMM_PATH");
