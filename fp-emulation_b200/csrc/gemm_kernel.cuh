@@ -426,19 +426,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 #pragma unroll
                         for (int j = 0; j < 16; ++j) { hi[j] = 0.0; lo[j] = 0.0; }
                         const uint8_t* src = scr + (int64_t)(h >> 1) * 1024 + (h & 1) * 16;
-                        // The staged residues of modulus m2 + 2 are loaded while modulus m2
-                        // is accumulated: with 8 epilogue warps per SM, one load per
-                        // modulus issued just before its use leaves the FP64 work waiting
-                        // on the memory latency.
-                        constexpr int64_t kPlane = (int64_t)kChunks * 1024;
-                        const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-                        uint4 q0 = __ldcs(reinterpret_cast<const uint4*>(src));
-                        uint4 q1 = P.n_mod > 1 ? __ldcs(reinterpret_cast<const uint4*>(src + kPlane)) : zero;
 #pragma unroll 1
                         for (int m2 = 0; m2 < P.n_mod; ++m2) {
-                            const uint4 q = q0;
-                            q0 = q1;
-                            q1 = m2 + 2 < P.n_mod ? __ldcs(reinterpret_cast<const uint4*>(src + (m2 + 2) * kPlane)) : zero;
+                            const uint4 q = *reinterpret_cast<const uint4*>(src + (int64_t)m2 * kChunks * 1024);
                             const double wh = P.cc.wh[m2], wm = P.cc.wm[m2], wl = P.cc.wl[m2];
                             const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
