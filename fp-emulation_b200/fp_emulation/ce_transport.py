@@ -27,7 +27,10 @@ from __future__ import annotations
 
 import atexit
 import os
+import time
+from multiprocessing import shared_memory
 
+import numpy as np
 import torch
 import torch.distributed as dist
 from cuda.bindings import runtime as rt
@@ -305,35 +308,89 @@ class CeChain(_IpcChunks):
         self._wait(stream, self._done(self.rank, c, self.pieces - 1), "wait chunk")
 
 
+class _Positions:
+    """How far each rank of the group has enqueued its transport work: one
+    monotonic int64 per rank in a shared-memory block that every rank of the
+    node maps (the products run one process per GPU on one node).  A rank
+    publishes the position of each item after enqueuing it; a rank about to
+    enqueue a stream wait on a peer's event first waits until the peer's
+    position shows that the matching record is enqueued.  Reading a shared word
+    costs about a microsecond where a store round trip costs tens, so the ring
+    can order its enqueues per (chunk, step).  Host waits are bounded
+    (FPEMU_HOST_WAIT_S, default 120 s) and raise instead of hanging."""
+
+    def __init__(self, group, rank, world, tag):
+        self.rank = rank
+        self.timeout = float(os.environ.get("FPEMU_HOST_WAIT_S", "120"))
+        name = f"fpemu_pos_{os.getpid()}_{tag}"
+        self._own = shared_memory.SharedMemory(create=True, size=8, name=name)
+        np.ndarray((1,), dtype=np.int64, buffer=self._own.buf)[0] = -1
+        names = [None] * world
+        dist.all_gather_object(names, name, group=group)
+        self._blocks = [self._own if r == rank else shared_memory.SharedMemory(name=n) for r, n in enumerate(names)]
+        self._views = [np.ndarray((1,), dtype=np.int64, buffer=b.buf) for b in self._blocks]
+
+    def publish(self, pos):
+        self._views[self.rank][0] = pos
+
+    def wait(self, r, pos, what=""):
+        v = self._views[r]
+        if v[0] >= pos:
+            return
+        t0 = time.monotonic()
+        while v[0] < pos:
+            if time.monotonic() - t0 > self.timeout:
+                raise RuntimeError(f"rank {self.rank}: rank {r} did not enqueue {what} (position {pos}, at {v[0]}) "
+                                   f"within {self.timeout:.0f} s")
+            time.sleep(2e-5)
+
+    def close(self):
+        views, self._views = self._views, []
+        del views
+        for b in self._blocks:
+            try:
+                b.close()
+            except Exception:
+                pass
+        try:
+            self._own.unlink()
+        except Exception:
+            pass
+        self._blocks = []
+
+
 class CeRing(_IpcChunks):
     """Every rank splits one strip of each chunk; the residue strips then go
-    round a ring by the copy engines.  Opt-in: bit-exact on 2 GPUs, not yet
-    measured or run on more (its enqueue protocol is checked on 2-4 CPU ranks
-    with a fake runtime).
+    round a ring by the copy engines, chunk after chunk.
 
     Ranks form the ring order = root, root+1, ...; pred/succ are the neighbours
-    in it.  Per call and chunk c:
-      root, copy stream:    FP64 strip q of B -> rank q's staging slot c (2-D copy
-                            into the peer's buffer), then record stage[c];
-      rank r, split stream: wait the root's stage[c], split its own strip into
-                            its residue buffer, record have[c][r];
-      rank r, ring step t (1 .. W-1, one stream per step): the strip s that is t
-                            positions behind r in the ring is in pred's buffer
-                            once pred's have[c][s] fires (pred's own split for
-                            t = 1, its step t-1 otherwise): copy it, record
-                            have[c][s];
-      GEMM on chunk c:      after have[c][q] for every q.
+    in it.  Per call, for each chunk c in order:
+      root, copy stream:   (staged) FP64 strip q of B -> rank q's staging slot c
+                           (2-D copy into the peer's buffer), then record stage[c];
+      rank r, split stream: (staged: after the root's stage[c]) split its own
+                           strip into its residue buffer, record have[c][r];
+      rank r, ring stream: for step t = 1 .. W-1, the strip s that is t positions
+                           behind r is in pred's buffer once pred's have[c][s]
+                           fires (pred's split for t = 1, its step t-1
+                           otherwise): copy it, in `pieces` groups of modulus
+                           planes, each recorded as have[c][s][piece];
+      GEMM on chunk c:     after have[c][q] for every q.
+    All steps of a chunk go before the next chunk on the one ring stream, so
+    every hop of chunk c has the link to itself: chunk 0 arrives after W-1 hops
+    (in pieces) and the others follow one per chunk transfer time, instead of
+    all chunks advancing together and arriving together.
     Reuse across calls: the root overwrites slot c after every rank's split of
-    the previous call read it (have[c][q] on rank q); r overwrites its strip s
-    of chunk c after its own GEMM of the previous call and, unless s is succ's
-    own strip, after succ pulled it (succ's have[c][s]).
-    Host phases, each published as a key once its records are enqueued: "stage"
-    (root), "split", "ring1" .. "ring{W-1}"; before enqueuing a wait, a rank
-    waits for the key of the phase that enqueued the matching record.  Every
-    dependency points to an earlier phase of the same call or to the previous
-    call, so the phases never wait in a circle, and a stream wait always binds
-    to the intended record: the peer cannot enqueue its next record of that
-    event before the waiting rank has published the phase holding the wait."""
+    the previous call read it; r overwrites its strip s of chunk c after its own
+    GEMM of the previous call and, unless s is succ's own strip, after succ
+    pulled it.
+    Host order: item (call, c, k) -- k = 0 stage, 1 split, 1 + t ring step t --
+    has position ((call * chunks) + c) * (W + 1) + k; each rank publishes its
+    position after enqueuing an item (_Positions) and, before enqueuing a wait
+    on a peer's record, waits until the peer has published the item holding that
+    record.  Every wait points to an item of an earlier chunk, an earlier step of
+    the same chunk on the predecessor, or the previous call, so the ranks never
+    wait in a circle, and the peer cannot enqueue its next record of an event
+    before this rank has enqueued its wait on the current one."""
 
     EVENTS = ("stage", "have")
 
@@ -342,9 +399,7 @@ class CeRing(_IpcChunks):
         own copy of its part of B (a column-sharded B), and only the ring moves
         data between GPUs.  `pieces` (FPEMU_RING_PIECES, default 4): each ring
         step moves a strip as that many groups of modulus planes, each with its
-        own event, so the next hop starts on the first group instead of waiting
-        for the whole strip (the first chunk's fill shrinks from W-1 strip copies
-        to W-1 piece copies plus one strip)."""
+        own event, so the next hop starts on the first group."""
         self.layout = layout
         self.staged = staged
         P = int(os.environ.get("FPEMU_RING_PIECES", "4")) if pieces is None else pieces
@@ -358,14 +413,17 @@ class CeRing(_IpcChunks):
         self.succ = self.order[(self.pos + 1) % W]
         self.split_stream = self._new_stream()
         self.copy_stream = self._new_stream()
-        self.ring = [self._new_stream() for _ in range(W - 1)]  # step t on ring[t - 1]
-        self.phases = (("stage",) if staged else ()) + ("split",) + tuple(f"ring{t}" for t in range(1, W))
+        self.ring_stream = self._new_stream()
+        self.board = self._positions(group)
+
+    def _positions(self, group):
+        return _Positions(group, self.rank, self.world, self.key_prefix.replace("/", "_"))
 
     def _events_per_chunk(self, name):
         return self.world * self.pieces if name == "have" else 1
 
     def _phases(self):
-        return self.phases
+        return ()
 
     def _have(self, owner, c, q, p=None):
         """Event `owner` records once piece p of strip q of chunk c is in its buffer;
@@ -390,69 +448,63 @@ class CeRing(_IpcChunks):
     def _base(self, r):
         return int(self.ptr) if r == self.rank else self.peer_ptr(r)
 
+    def _at(self, call, c, k):
+        return (call * len(self.layout.plan) + c) * (self.world + 1) + k
+
     # -- per call ---------------------------------------------------------------
-    def root_stage(self, B_ptr, ldb, main_stream):
-        """Root: FP64 strips of every chunk into every rank's staging slots.
-        B_ptr/ldb: the root's B (row-major, ldb doubles per row)."""
+    def enqueue(self, split_fn, main_stream, B_ptr=None, ldb=None):
+        """Enqueue this call's transport: per chunk, the root's staging (staged:
+        B_ptr/ldb, the root's row-major B), every rank's split of its strip
+        (split_fn(c, stream) enqueues it on `stream`), and the ring steps.  The
+        split stream (unstaged) and the root's copy stream (staged) first wait for
+        `main_stream`, where the caller produced B."""
         i = self.calls
         L = self.layout
-        if i > 0:
-            self._wait_keys(self.order, i - 1, "split")
-        cs = self.copy_stream
-        cs.wait_stream(main_stream)
-        for c, (c0, _c1) in enumerate(L.plan):
-            if i > 0:
-                for q in range(self.world):
-                    self._wait(cs, self._have(q, c, q), "stage war")
-            for q, (s0, s1) in enumerate(L.strips[c]):
-                if s1 > s0:
-                    self._copy2d(cs, self._base(q) + L.stage_off + c * L.slot_bytes, L.pitch * 8,
-                                 B_ptr + (c0 + s0) * 8, ldb * 8, (s1 - s0) * 8, L.k)
-            self._record(cs, self._stage(c))
-        self._publish("stage")
-
-    def split_own(self, split_fn, main_stream=None):
-        """Every rank: split_fn(c, stream) enqueues on `stream` the split of this
-        rank's FP64 strip of chunk c (staging slot c, or the rank's own part of B
-        when unstaged) into its residue strip.  Unstaged, the split stream first
-        waits for `main_stream`, where the caller produced its part of B."""
-        i = self.calls
-        if self.staged:
-            self._wait_keys([self.root], i, "stage")
-        if i > 0 and self.world > 1:
-            self._wait_keys([self.succ], i - 1, "ring1")
-        ss = self.split_stream
-        if not self.staged and main_stream is not None:
+        W = self.world
+        board, at = self.board, self._at
+        ss, rs, cs = self.split_stream, self.ring_stream, self.copy_stream
+        if self.staged and self.rank == self.root:
+            cs.wait_stream(main_stream)
+        if not self.staged:
             ss.wait_stream(main_stream)
-        for c in range(len(self.layout.plan)):
+        pieces = self.plane_pieces()
+        for c, (c0, c1) in enumerate(L.plan):
+            w = c1 - c0
+            base = c * L.chunk_bytes
+            # Root: this chunk's FP64 strips into every rank's staging slot c.
+            if self.staged and self.rank == self.root:
+                if i > 0:
+                    for q in range(W):
+                        board.wait(q, at(i - 1, c, 1), "its previous split")
+                        self._wait(cs, self._have(q, c, q), "stage war")
+                for q, (s0, s1) in enumerate(L.strips[c]):
+                    if s1 > s0:
+                        self._copy2d(cs, self._base(q) + L.stage_off + c * L.slot_bytes, L.pitch * 8,
+                                     B_ptr + (c0 + s0) * 8, ldb * 8, (s1 - s0) * 8, L.k)
+                self._record(cs, self._stage(c))
+                board.publish(at(i, c, 0))
+            # Every rank: split its own strip of chunk c.
             ss.wait_event(self.gemm_done[c])
             if self.staged:
+                board.wait(self.root, at(i, c, 0), "the staging")
                 self._wait(ss, self._stage(c), "stage")
-            if i > 0 and self.world > 1:  # succ pulled this strip at its step 1
+            if i > 0 and W > 1:  # succ pulled this strip at its step 1 of the previous call
+                board.wait(self.succ, at(i - 1, c, 2), "its previous step 1")
                 self._wait(ss, self._have(self.succ, c, self.rank), "split war")
             split_fn(c, ss)
             for p in range(self.pieces):  # the split wrote every piece of this rank's strip
                 self._record(ss, self._have(self.rank, c, self.rank, p))
-        self._publish("split")
-
-    def ring_steps(self):
-        """Every rank: pull the W-1 other strips of every chunk round the ring."""
-        i = self.calls
-        L = self.layout
-        W = self.world
-        for t in range(1, W):
-            self._wait_keys([self.pred], i, "split" if t == 1 else f"ring{t - 1}")
-            war = i > 0 and t < W - 1  # succ pulls this strip from us at its step t+1
-            if war:
-                self._wait_keys([self.succ], i - 1, f"ring{t + 1}")
-            rs = self.ring[t - 1]
-            s = self.strip_at(t)
-            pieces = self.plane_pieces()
-            for c, (c0, c1) in enumerate(L.plan):
+            board.publish(at(i, c, 1))
+            # Every rank: the W-1 other strips of chunk c round the ring.
+            if W > 1:
                 rs.wait_event(self.gemm_done[c])
+            for t in range(1, W):
+                s = self.strip_at(t)
+                board.wait(self.pred, at(i, c, 1 if t == 1 else t), f"step {t - 1} of chunk {c}")
+                war = i > 0 and t < W - 1  # succ pulls this strip from us at its step t+1
+                if war:
+                    board.wait(self.succ, at(i - 1, c, t + 2), f"its previous step {t + 1}")
                 s0, s1 = L.strips[c][s]
-                w = c1 - c0
-                base = c * L.chunk_bytes
                 for p, (l0, l1) in enumerate(pieces):
                     self._wait(rs, self._have(self.pred, c, s, p), "ring")
                     if war:
@@ -466,17 +518,26 @@ class CeRing(_IpcChunks):
                             off = base + L.res_bytes + 4 * s0  # column exponents
                             self._copy(rs, int(self.ptr) + off, self.peer_ptr(self.pred) + off, 4 * (s1 - s0))
                     self._record(rs, self._have(self.rank, c, s, p))
-            self._publish(f"ring{t}")
-        # Every rank that waits on this rank's keys of call i-2 has passed those
-        # waits (they sit in calls i-2 and i-1 of the neighbours and the root,
-        # whose later keys this rank has just waited for).
-        self._forget(i - 2, self.phases)
+                board.publish(at(i, c, 1 + t))
         self.calls += 1
 
     def wait_chunk(self, c, stream):
         """`stream` waits until every strip of chunk c is in this rank's buffer."""
         for q in range(self.world):
             self._wait(stream, self._have(self.rank, c, q), "gemm")
+
+    def release(self, barrier):
+        super().release(barrier)
+        if self.board is not None:
+            self.board.close()
+            self.board = None
+
+    def close(self):
+        super().close()
+        board = getattr(self, "board", None)
+        if board is not None:
+            board.close()
+            self.board = None
 
 
 TRANSPORTS = {"ce": CeChain, "ce-ring": CeRing}

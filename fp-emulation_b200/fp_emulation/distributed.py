@@ -41,8 +41,8 @@ BCAST_MODE = os.environ.get("FPEMU_BCAST", "residues")
 #  "ce" (default): the root splits B, copy engines relay the chunks along a chain
 #         of ranks through CUDA IPC (ce_transport.py);
 #  "ce-ring": every rank splits a strip of each chunk (FP64 strips copied from the
-#         root), the residue strips go round a ring by the copy engines
-#         (ce_transport.CeRing); bit-exact on 2 GPUs, not yet measured;
+#         root), the residue strips go round a ring by the copy engines, chunk
+#         after chunk (ce_transport.CeRing);
 #  "nccl": the root splits B, NCCL broadcast kernels move the chunks.
 TRANSPORT = os.environ.get("FPEMU_TRANSPORT", "ce")
 
@@ -218,8 +218,8 @@ def _align256(x):
 def rowsharded_product_ring(A_local, B, n, k, bits, n_mod, ops, root=0, group=None, chunk_cols=CHUNK_COLS):
     """Same product through the copy-engine ring (ce_transport.CeRing): the root
     copies each rank its FP64 strip of every chunk, every rank splits its strip,
-    and the residue strips go round the ring by the copy engines.  Opt-in
-    (FPEMU_TRANSPORT=ce-ring): bit-exact on 2 GPUs, not yet measured."""
+    and the residue strips go round the ring by the copy engines, chunk after
+    chunk (FPEMU_TRANSPORT=ce-ring)."""
     from fp_emulation.ce_transport import CeRing
     from fp_emulation.strips import StripLayout
 
@@ -237,10 +237,10 @@ def rowsharded_product_ring(A_local, B, n, k, bits, n_mod, ops, root=0, group=No
     def views(c):
         return L.chunk_views(tr.buf, c)
 
+    Bc = None
     if rank == root:
         Bc = B if B.stride(1) == 1 else B.contiguous()
         Bc.record_stream(tr.copy_stream)
-        tr.root_stage(Bc.data_ptr(), Bc.stride(0), stream)
 
     def split_fn(c, ss):
         s0, s1 = L.strips[c][rank]
@@ -251,8 +251,7 @@ def rowsharded_product_ring(A_local, B, n, k, bits, n_mod, ops, root=0, group=No
         with torch.cuda.stream(ss):
             ops.split(X, bits, n_mod, res[:, s0:s1, :], exps[s0:s1])
 
-    tr.split_own(split_fn)
-    tr.ring_steps()
+    tr.enqueue(split_fn, stream, Bc.data_ptr() if Bc is not None else None, Bc.stride(0) if Bc is not None else None)
     a_res = ops.empty_res(n_mod, m, ld)
     row_exp = ops.empty_exps(m)
     ops.split(A_local, bits, n_mod, a_res, row_exp)
@@ -377,8 +376,7 @@ def rowsharded_product_allgather(A_local, B_local, k, bits, n_mod, ops, group=No
         with torch.cuda.stream(ss):
             ops.split(X, bits, n_mod, res[:, s0:s1, :], exps[s0:s1])
 
-    tr.split_own(split_fn, main_stream=stream)
-    tr.ring_steps()
+    tr.enqueue(split_fn, stream)
     a_res = ops.empty_res(n_mod, m, ld)
     row_exp = ops.empty_exps(m)
     ops.split(A_local, bits, n_mod, a_res, row_exp)
