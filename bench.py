@@ -160,6 +160,49 @@ def dist_env():
     return world, rank, local
 
 
+def _cpulist(text):
+    cpus = set()
+    for part in text.strip().split(","):
+        if part:
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
+class near_gpu:
+    """Run a block on the CPUs of the GPU's NUMA node, so that host memory the
+    block allocates (pinned buffers of the end-to-end loop) is placed on the
+    node whose root complex the GPU hangs off: DMA then never crosses the
+    socket link.  The caller's affinity is restored on exit; pages keep their
+    placement.  Skipped (node None) where sysfs gives no node for the GPU."""
+
+    def __init__(self, torch, dev):
+        self.node, self.cpus = None, set()
+        try:
+            p = torch.cuda.get_device_properties(dev)
+            bdf = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            node = int(Path(f"/sys/bus/pci/devices/{bdf}/numa_node").read_text())
+            if node >= 0:
+                cpus = _cpulist(Path(f"/sys/devices/system/node/node{node}/cpulist").read_text())
+                self.cpus = cpus & os.sched_getaffinity(0)
+                self.node = node
+        except (OSError, ValueError, AttributeError):
+            pass
+
+    def __enter__(self):
+        self.saved = os.sched_getaffinity(0)
+        if self.cpus:
+            os.sched_setaffinity(0, self.cpus)
+        return self
+
+    def __exit__(self, *exc):
+        os.sched_setaffinity(0, self.saved)
+        return False
+
+    def describe(self):
+        return {"node": self.node, "cpus": len(self.cpus)}
+
+
 def measured_peaks():
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
@@ -426,9 +469,11 @@ def run_ours(args):
         # each rank copying in only its rows of A and its block of B's columns
         # (every GPU's PCIe link carries its share; B whole on one rank would put
         # all of B's bytes through the root's link every step).
-        A_h = A.cpu().pin_memory()
-        B_h = (B if world == 1 else B_block).cpu().pin_memory()
-        C_h = [torch.empty((m, n), dtype=torch.float64).pin_memory() for _ in range(2)]
+        numa = near_gpu(torch, dev)
+        with numa:
+            A_h = A.cpu().pin_memory()
+            B_h = (B if world == 1 else B_block).cpu().pin_memory()
+            C_h = [torch.empty((m, n), dtype=torch.float64).pin_memory() for _ in range(2)]
         A_d = [torch.empty_like(A) for _ in range(2)]
         B_d = [torch.empty(tuple(B_h.shape), dtype=torch.float64, device=dev) for _ in range(2)]
         del a_res  # give the public op's own workspace room
@@ -484,6 +529,9 @@ def run_ours(args):
         e2e = {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
                "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": int(d2h_bytes),
                "ms_per_step": round(e2e_ms, 3),
+               "host_buffers": "pinned, allocated on the GPU's NUMA node" if numa.node is not None
+                               else "pinned (no NUMA node reported for the GPU)",
+               "numa": numa.describe(),
                "method": ("public op per step" if world == 1 else
                           "column-sharded public op (ozaki2_int8_matmul_allgather) per step: each rank copies in "
                           "its rows of A and its column block of B") +
