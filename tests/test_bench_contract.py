@@ -105,3 +105,31 @@ def test_parity_gate_passes_on_correct_shards_and_raises_everywhere_on_one_ulp()
     assert all(st == "ok" and msg == "bit-exact" for st, msg in good.values()), good
     bad = _run_gate(plant=True)
     assert all(st == "raised" for st, _ in bad.values()), bad
+
+
+def test_host_buffer_numa_placement_helpers():
+    """The e2e loop's NUMA placement: cpulist parsing, and a GPU with no node in
+    sysfs (or no such PCI device here) leaves the affinity untouched."""
+    import os
+
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    assert bench._cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    assert bench._cpulist("") == set()
+
+    class Props:
+        pci_domain_id, pci_bus_id, pci_device_id = 0xFFFF, 0xFF, 0x1F
+
+    class FakeTorch:
+        class cuda:
+            @staticmethod
+            def get_device_properties(dev):
+                return Props()
+
+    before = os.sched_getaffinity(0)
+    placement = bench.near_gpu(FakeTorch, 0)
+    with placement:
+        assert os.sched_getaffinity(0) == before
+    assert placement.describe() == {"node": None, "cpus": 0}
+    assert os.sched_getaffinity(0) == before
