@@ -26,9 +26,9 @@ is World-1 hops deep, so its fill latency grows with the rank count.
 from __future__ import annotations
 
 import atexit
+import mmap
 import os
 import time
-from multiprocessing import shared_memory
 
 import numpy as np
 import torch
@@ -41,6 +41,9 @@ def _check(res, what):
     if err != rt.cudaError_t.cudaSuccess:
         raise RuntimeError(f"{what} failed: {err}")
     return res[1] if isinstance(res, tuple) and len(res) == 2 else res
+
+
+_SHM_DIR = "/dev/shm"  # node-local shared memory (tmpfs)
 
 
 def _align256(x):
@@ -323,12 +326,29 @@ class _Positions:
         self.rank = rank
         self.timeout = float(os.environ.get("FPEMU_HOST_WAIT_S", "120"))
         name = f"fpemu_pos_{os.getpid()}_{tag}"
-        self._own = shared_memory.SharedMemory(create=True, size=8, name=name)
-        np.ndarray((1,), dtype=np.int64, buffer=self._own.buf)[0] = -1
+        self._path = os.path.join(_SHM_DIR, name)
+        own = self._map(self._path, create=True)
+        np.ndarray((1,), dtype=np.int64, buffer=own)[0] = -1
         names = [None] * world
         dist.all_gather_object(names, name, group=group)
-        self._blocks = [self._own if r == rank else shared_memory.SharedMemory(name=n) for r, n in enumerate(names)]
-        self._views = [np.ndarray((1,), dtype=np.int64, buffer=b.buf) for b in self._blocks]
+        self._maps = [own if r == rank else self._map(os.path.join(_SHM_DIR, n)) for r, n in enumerate(names)]
+        self._views = [np.ndarray((1,), dtype=np.int64, buffer=m) for m in self._maps]
+        atexit.register(self.close)
+
+    @staticmethod
+    def _map(path, create=False):
+        # Plain files in the node's shared-memory file system, mapped directly:
+        # multiprocessing's SharedMemory would register peers' blocks with each
+        # process's resource tracker as if that process owned them.  Only the
+        # creating rank unlinks its block.
+        flags = os.O_RDWR | (os.O_CREAT | os.O_EXCL if create else 0)
+        fd = os.open(path, flags, 0o600)
+        try:
+            if create:
+                os.ftruncate(fd, 8)
+            return mmap.mmap(fd, 8)
+        finally:
+            os.close(fd)
 
     def publish(self, pos):
         self._views[self.rank][0] = pos
@@ -347,16 +367,16 @@ class _Positions:
     def close(self):
         views, self._views = self._views, []
         del views
-        for b in self._blocks:
+        for m in self._maps:
             try:
-                b.close()
+                m.close()
             except Exception:
                 pass
+        self._maps = []
         try:
-            self._own.unlink()
-        except Exception:
+            os.unlink(self._path)
+        except OSError:
             pass
-        self._blocks = []
 
 
 class CeRing(_IpcChunks):
