@@ -230,7 +230,7 @@ def test_chain_waits_bind_to_the_right_records(world, root):
 _PREVIOUS_CALL = {"stage war", "split war", "ring war", "gemm"}
 
 
-def _ring_worker(rank, world, port, root, calls, n_chunks, q, staged=True):
+def _ring_worker(rank, world, port, root, calls, n_chunks, q, staged=True, pieces=None):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         import torch.distributed as dist
@@ -271,7 +271,7 @@ def _ring_worker(rank, world, port, root, calls, n_chunks, q, staged=True):
         else:  # column blocks of 90 columns, strips of 32: chunks of 32, 32 and 26 per rank
             layout = StripLayout.for_blocks(world, 300, 24, 304, 32 * n_chunks - 6, 32)
             plan = layout.plan
-        ring = FakeRing(None, root, None, layout, staged=staged)
+        ring = FakeRing(None, root, None, layout, staged=staged, pieces=pieces)
         fake.chain = ring
         splits = []
         main = _Stream()
@@ -292,9 +292,10 @@ def _ring_worker(rank, world, port, root, calls, n_chunks, q, staged=True):
         q.put((rank, "error", traceback.format_exc()))
 
 
+@pytest.mark.parametrize("pieces", [None, 4], ids=["default-pieces", "4-pieces"])
 @pytest.mark.parametrize("staged", [True, False], ids=["root-staged", "column-sharded"])
 @pytest.mark.parametrize("world,root", [(2, 1), (3, 0), (4, 3)])
-def test_ring_waits_bind_to_the_right_records(world, root, staged):
+def test_ring_waits_bind_to_the_right_records(world, root, staged, pieces):
     """Root-staged: the root copies every rank its FP64 strip.  Column-sharded
     (the all-gather product): every rank splits its own block, nothing is staged."""
     calls, n_chunks = 4, 3
@@ -303,7 +304,7 @@ def test_ring_waits_bind_to_the_right_records(world, root, staged):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ring_worker, args=(r, world, port, root, calls, n_chunks, q, staged))
+    procs = [ctx.Process(target=_ring_worker, args=(r, world, port, root, calls, n_chunks, q, staged, pieces))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -330,7 +331,7 @@ def test_ring_waits_bind_to_the_right_records(world, root, staged):
         assert n_splits == nc * calls
         # 2-D copies: the root's FP64 strips (W per chunk) and the ring's residue strips;
         # 1-D copies: the ring's column exponents.
-        assert P == 4
+        assert P == (4 if pieces == 4 else 1)
         assert copies2d == (W * nc * calls if rank == root and staged else 0) + (W - 1) * nc * calls * P
         assert copies == (W - 1) * nc * calls
         assert left == [], left
