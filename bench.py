@@ -90,6 +90,8 @@ def workload_config(args, n_mod, world, transport=None):
             f"({transport or os.environ.get('FPEMU_TRANSPORT', 'ce')}"
             f"{'' if 'column-sharded' in str(transport) else ' transport, B on rank 0'}, "
             f"{os.environ.get('FPEMU_BCAST', 'residues')})"),
+        **({} if world == 1 else {"pieces": {"chain_per_chunk": int(os.environ.get("FPEMU_CE_PIECES", "8")),
+                                             "ring_per_strip": int(os.environ.get("FPEMU_RING_PIECES", "1"))}}),
     }
 
 

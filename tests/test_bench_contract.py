@@ -39,9 +39,11 @@ def test_workload_configs():
     assert bench.problem_shape(a) == (131072, 8192, 8192)
     c = bench.workload_config(a, 25, 8, "ce")
     assert c["m"] == 131072 and c["k"] == 8192 and "ce transport" in c["parallelism"] and "phi" not in c
+    assert set(c["pieces"]) == {"chain_per_chunk", "ring_per_strip"}
     a = argparse.Namespace(config=2, n=16384, phi=1.0)
     c = bench.workload_config(a, 25, 1)
     assert (c["m"], c["n"], c["k"], c["phi"], c["parallelism"]) == (16384, 16384, 16384, 1.0, "single GPU")
+    assert "pieces" not in c
 
 
 def _gate_worker(rank, world, port, plant, q):
