@@ -342,7 +342,13 @@ class _Positions:
         # process's resource tracker as if that process owned them.  Only the
         # creating rank unlinks its block.
         flags = os.O_RDWR | (os.O_CREAT | os.O_EXCL if create else 0)
-        fd = os.open(path, flags, 0o600)
+        try:
+            fd = os.open(path, flags, 0o600)
+        except FileExistsError:
+            # Names carry the creator's pid and a per-process serial, so an
+            # existing file was left by a dead process that had this pid.
+            os.unlink(path)
+            fd = os.open(path, flags, 0o600)
         try:
             if create:
                 os.ftruncate(fd, 8)

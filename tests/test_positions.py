@@ -74,3 +74,19 @@ def test_positions_board_orders_times_out_and_cleans_up(tmp_path):
     assert out.returncode == 0, out.stderr[-3000:]
     assert out.stdout.strip().splitlines()[-1] == "['saw 5', 'timeout']"
     assert "resource_tracker" not in out.stderr, out.stderr[-3000:]
+
+
+def test_board_block_replaces_a_stale_file(tmp_path):
+    """A block left by a dead process with the same pid is replaced, not an error."""
+    import numpy as np
+
+    from fp_emulation.ce_transport import _Positions
+
+    path = tmp_path / "fpemu_pos_stale"
+    path.write_bytes(b"\xff" * 8)
+    m = _Positions._map(str(path), create=True)
+    np.ndarray((1,), dtype=np.int64, buffer=m)[0] = 7
+    peer = _Positions._map(str(path))
+    assert int(np.ndarray((1,), dtype=np.int64, buffer=peer)[0]) == 7
+    peer.close()
+    m.close()
